@@ -1,0 +1,419 @@
+"""Benchmark: block-sparse prefill effective TFLOP/s (+ decode tok/s) at the Llama-3-8B
+attention shape with 80% block sparsity, on N B200 GPUs (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: prefill bf16 B=4 (per GPU), 32 q-heads /
+8 kv-heads, S=4096, D=128, block 64, causal, mask from the random-init AttnGate's fp32
+scores (kv-head max, row rule of ``tasft_b200.masks.prefill_mask`` at density 0.2);
+decode bf16 batch 64 (per GPU), KV 8192, 26 kept blocks per (sequence, kv-head).
+Work is partitioned by batch, so N GPUs process N independent shards ("weak" scaling,
+no data-path collective). Each timed step is bracketed by CUDA events on the launching
+stream; L2 is flushed (a 256 MiB write) before every timed step, outside the events.
+
+``value`` = kept-block FLOPs of all ranks / max-over-ranks device time of the step
+``mask -> kept lists -> tcgen05 prefill``. ``e2e`` = the same metric through
+``BlockSparseFlashAttention.forward`` with pinned host inputs (H2D q, k, v, mask and D2H
+of the output inside the timed region). ``--impl reference`` times the CPU oracle (the
+restatement of the reference kernel) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "prefill effective TFLOP/s + decode tok/s, Llama-3-8B attn @80% sparsity"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+CFG = dict(B=4, Hq=32, Hk=8, S=4096, D=128, block=64, density=0.2)
+DEC = dict(B=64, Hq=32, Hk=8, L=8192, D=128, block=64, density=0.2)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {**PEAKS_FALLBACK, "src": "fallback"}
+
+
+def load_traffic():
+    p = ROOT / "profiles" / "traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (clocks + throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, ws, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist  # noqa: PLC0415
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist  # noqa: PLC0415
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+def make_prefill_inputs(seed: int, dev):
+    import tasft_b200 as T  # noqa: PLC0415
+    from tasft_b200 import masks as M  # noqa: PLC0415
+
+    c = CFG
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(c["B"], c["Hq"], c["S"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(c["B"], c["Hk"], c["S"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(c["B"], c["Hk"], c["S"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    torch.manual_seed(0)
+    gate = T.AttnGate(c["Hq"], c["D"], block_size=c["block"]).to(dev)
+    with torch.no_grad():
+        out = gate(q, k)
+    scores = M.group_max(out.soft_scores, c["Hk"])  # fp32, per kv-head
+    mask = M.prefill_mask(scores, c["density"])      # [B, Hk, NB, NB]
+    return q, k, v, mask, gate
+
+
+def make_decode_inputs(seed: int, dev):
+    import tasft_b200 as T  # noqa: PLC0415
+    from tasft_b200 import masks as M  # noqa: PLC0415
+
+    c = DEC
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(c["B"], c["Hq"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    kc = torch.randn(c["B"], c["Hk"], c["L"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    vc = torch.randn(c["B"], c["Hk"], c["L"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    kv_len = torch.full((c["B"],), c["L"], dtype=torch.int32, device=dev)
+    torch.manual_seed(0)
+    gate = T.AttnGate(c["Hq"], c["D"], block_size=c["block"]).to(dev)
+    with torch.no_grad():
+        sc = gate(q.unsqueeze(2), kc).soft_scores[:, :, 0, :]  # query pooled with the 1-token padding
+    nb = c["L"] // c["block"]
+    mask = M.decode_mask(M.group_max(sc, c["Hk"]), (kv_len + 63) // 64, c["density"], nb)
+    idx, cnt = M.lists_from_mask(mask)
+    return q, kc, vc, kv_len, T.KeptBlocks(idx, cnt)
+
+
+class L2Flush:
+    def __init__(self, dev):
+        self.buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def time_steps(fn, steps, warmup, flush, ws):
+    for _ in range(warmup):
+        flush()
+        fn()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    times = []
+    for _ in range(steps):
+        flush()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        fn()
+        e1.record(st)
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in times]
+
+
+# ---------------------------------------------------------------------------
+def cpu_prefill_sample(budget_s: float = 10.0):
+    """Oracle (reference restatement) on host cores: (b, kv-head) chunks of the C2 workload."""
+    import oracle as O  # noqa: PLC0415  (CPU baseline leg)
+    from tasft_b200 import masks as M  # noqa: PLC0415
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = CFG
+    grp = c["Hq"] // c["Hk"]
+    g = torch.Generator().manual_seed(1234)
+    nb = c["S"] // c["block"]
+    q = torch.randn(1, grp, c["S"], c["D"], generator=g).to(torch.bfloat16)
+    k = torch.randn(1, 1, c["S"], c["D"], generator=g).to(torch.bfloat16)
+    v = torch.randn(1, 1, c["S"], c["D"], generator=g).to(torch.bfloat16)
+    mask = M.prefill_mask(torch.rand(1, 1, nb, nb, generator=g), c["density"])
+    flops_chunk = int(mask.sum()) * grp * 4 * c["block"] * c["block"] * c["D"]
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        O.bsa_prefill_masked_dense(q, k, v, mask, c["block"])
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(flops_chunk * n / dt / 1e12, 6), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} x one (batch, kv-head) chunk = {grp} q-heads, S={c['S']}, D={c['D']}, "
+                      f"{int(mask.sum())} kept blocks; oracle masked-dense restatement in bf16/fp32 "
+                      f"(oracle/tasft_oracle.py:bsa_prefill_masked_dense), {dt:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    budget = 3.0
+    for _ in range(max(args.warmup, 0)):
+        cpu_prefill_sample(budget_s=0.0)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        vals.append(cpu_prefill_sample(budget_s=budget))
+    wall = time.perf_counter() - t0
+    v = statistics.median([x["value"] for x in vals])
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "llama3-8b attention prefill, B=4 Hq=32 Hk=8 S=4096 D=128 block=64, 80% sparsity "
+                               "(CPU sample: one (batch, kv-head) chunk per step)", "model": "llama3-8b-attn"},
+        "cpu_baseline": {**vals[0], "value": v},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import tasft_b200 as T  # noqa: PLC0415
+    from tasft_b200 import _lib as L  # noqa: PLC0415
+
+    rank, ws, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if ws > 1 else 0)
+    peaks = load_peaks()
+    traffic = load_traffic()
+    flush = L2Flush(dev)
+    kern = T.BlockSparseFlashAttention(block_size=CFG["block"])
+
+    # ---------------- prefill (value) ----------------
+    q, k, v, mask, _gate = make_prefill_inputs(1234 + 2 + 1000 * rank, dev)
+    kept_blocks = int(mask.sum().item())
+    grp = CFG["Hq"] // CFG["Hk"]
+    flops = kept_blocks * grp * 4 * CFG["block"] * CFG["block"] * CFG["D"]
+    out = torch.empty_like(q)
+
+    def step():
+        kern.forward(q, k, v, mask, out=out)
+
+    n0 = L.launch_count()
+    with ClockSampler(local) as clk:
+        t_step = time_steps(step, args.steps, args.warmup, flush, ws)
+    launches = (L.launch_count() - n0) // (args.steps + args.warmup)
+    ms = statistics.mean(t_step)
+    ms_max = max_over_ranks(ms, ws)
+    total_flops = sum_over_ranks(float(flops), ws)
+    value = total_flops / (ms_max * 1e-3) / 1e12
+
+    # kernel-only roofline: prefill kernel on prebuilt kept lists
+    kept = T.mask_to_kept(mask, True)
+    t_kern = time_steps(lambda: kern.forward(q, k, v, kept, out=out), args.steps, args.warmup, flush, ws)
+    ms_k = statistics.mean(t_kern)
+    achieved = flops / (ms_k * 1e-3) / 1e12
+    tr = traffic.get("prefill")
+    roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": tr,
+                "peak_src": f"bf16 burst, {peaks['src']}", "kernel": "bsa_prefill_tc_kernel",
+                "algorithmic": f"{flops / 1e9:.2f} GFLOP per launch (kept blocks x 4*64*64*128 x 4 q-heads)",
+                "ms_per_launch": round(ms_k, 4)}
+
+    # ---------------- e2e through the public API with host buffers ----------------
+    qh = q.cpu().pin_memory()
+    kh = k.cpu().pin_memory()
+    vh = v.cpu().pin_memory()
+    mh = mask.cpu().pin_memory()
+    oh = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+
+    def step_e2e():
+        qd = qh.to(dev, non_blocking=True)
+        kd = kh.to(dev, non_blocking=True)
+        vd = vh.to(dev, non_blocking=True)
+        md = mh.to(dev, non_blocking=True)
+        o = kern.forward(qd, kd, vd, md)
+        oh.copy_(o, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    t_e2e = time_steps(step_e2e, e2e_steps, max(args.warmup, 3), flush, ws)
+    ms_e2e = max_over_ranks(statistics.mean(t_e2e), ws)
+    h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2 + mh.numel()
+    d2h = oh.numel() * 2
+    del qh, kh, vh, oh, mh, q, k, v, out, kept
+
+    # ---------------- decode ----------------
+    qd, kc, vc, kv_len, dkept = make_decode_inputs(1234 + 3 + 1000 * rank, dev)
+    mean_kept = float(dkept.cnt.float().mean().item())
+    splits = T.decode.default_splits(DEC["B"], DEC["Hk"], mean_kept)
+    wsp = T.DecodeWorkspace(DEC["B"], DEC["Hq"], DEC["Hk"], DEC["D"], max(splits, 1), dev)
+    od = torch.empty_like(qd)
+
+    def dstep():
+        T.bsa_decode(qd, kc, vc, kv_len, dkept, DEC["block"], num_splits=splits, workspace=wsp, out=od)
+
+    t_dec = time_steps(dstep, args.steps, args.warmup, flush, ws)
+    ms_d = statistics.mean(t_dec)
+    ms_d_max = max_over_ranks(ms_d, ws)
+    kept_dec = int(dkept.cnt.sum().item())
+    dbytes = kept_dec * 2 * DEC["block"] * DEC["D"] * 2 + qd.numel() * 2 * 2
+    gbs = dbytes / (ms_d * 1e-3) / 1e9
+    tok_s = sum_over_ranks(DEC["B"], ws) / (ms_d_max * 1e-3)
+    decode = {"tok_s": round(tok_s, 1), "ms_per_step": round(ms_d_max, 4), "splits": splits,
+              "kept_blocks_per_seq_head": round(mean_kept, 2),
+              "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                           "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": traffic.get("decode"),
+                           "peak_src": peaks["src"], "kernel": "bsa_decode_kernel",
+                           "algorithmic": f"{dbytes / 1e6:.1f} MB per launch (kept K+V blocks + q + out)"}}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = cpu_prefill_sample(budget_s=args.cpu_budget)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "llama3-8b attention prefill (BASELINE configs[1]): B=4 per GPU, Hq=32, Hk=8, "
+                                   "S=4096, D=128, block=64, causal, 80% block sparsity (kv-head masks from the "
+                                   "random-init AttnGate's fp32 scores); decode configs[2] alongside",
+                       "model": "llama3-8b-attn", "global_batch": CFG["B"] * ws, "seq_len": CFG["S"],
+                       "parallelism": f"dp{ws} (batch shards, no collective)",
+                       "l2": "flushed (256 MiB write) before every timed step",
+                       "kept_blocks_per_gpu": kept_blocks, "gflop_per_gpu_step": round(flops / 1e9, 3)},
+            "roofline": roofline,
+            "e2e": {"value": round(total_flops / (ms_e2e * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 3),
+                    "api": "tasft_b200.BlockSparseFlashAttention.forward(q, k, v, bool mask) from pinned host"},
+            "decode": decode,
+            "gpu_launches": launches * args.steps,
+            "gpu_launches_per_step": launches,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

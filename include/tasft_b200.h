@@ -1,0 +1,264 @@
+/*
+ * tasft_b200.h -- C ABI of libtasft_b200.so, the B200 (sm_100a) implementation of
+ * TASFT's gated block-sparse attention path.
+ *
+ * Conventions
+ *   - Every pointer in an args struct is a DEVICE pointer unless its comment says
+ *     otherwise. The caller owns every buffer, including the workspace whose size
+ *     the matching *_workspace_size() call returns. The library keeps no allocation.
+ *   - Strides are in ELEMENTS (int64). Tensors are 4-D [batch, heads, seq, dim]
+ *     unless stated; the innermost (dim) stride must be 1.
+ *   - Launches are asynchronous on the given stream; no call synchronises the host.
+ *   - Return value: TASFT_OK (0) or a negative status for an argument error found on
+ *     the host before anything is launched. Errors that only the device can see
+ *     (an index out of range, a bounded wait that ran out) are OR-ed into the
+ *     optional `err` word (TASFT_DEVERR_* bits) and never trap the GPU.
+ *
+ * Reference interfaces replaced (v-code01/tasft, paths inside that project):
+ *   tasft_gate_mask_build      AttnGate.forward           tasft/modules/attn_gate.py:377-485
+ *   tasft_mask_from_scores     soft >= tau (+ tril)       tasft/modules/attn_gate.py:466-477
+ *   tasft_mask_to_kept         bool mask & block tril     tasft/kernels/block_sparse_fa.py:497-508
+ *   tasft_bsa_prefill_fwd      _block_sparse_attn_fwd_kernel launch
+ *                                                         tasft/kernels/block_sparse_fa.py:454-552
+ *   tasft_bsa_decode_fwd       (none: new capability; the reference delegates decode
+ *                              to vLLM's dense forward, tasft/inference/vllm_patch.py:189-196)
+ *   tasft_bsa_decode_combine   (none: split-KV (m,l,o) merge for multi-GPU decode)
+ *   tasft_gate_target_fwd      TASFTAttention scores + compute_gate_target
+ *                              tasft/modules/tasft_attention.py:427-458,
+ *                              tasft/training/objectives.py:128-185
+ *   tasft_gate_loss_fwd_bwd    compute_gate_loss + compute_sparsity_loss (+ grad)
+ *                              tasft/training/objectives.py:187-241
+ *   tasft_gate_bwd             autograd of AttnGate.forward to its parameters
+ *                              tasft/modules/attn_gate.py:442-459
+ */
+#ifndef TASFT_B200_H_
+#define TASFT_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TASFT_API __attribute__((visibility("default")))
+#else
+#define TASFT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TASFT_ABI_VERSION 1
+
+/* status codes (host-side, returned) */
+#define TASFT_OK                  0
+#define TASFT_ERR_INVALID_ARG    -1  /* null pointer, bad shape, bad stride */
+#define TASFT_ERR_UNSUPPORTED    -2  /* dtype / head_dim / block size not built */
+#define TASFT_ERR_CUDA           -3  /* a CUDA runtime call failed */
+#define TASFT_ERR_WORKSPACE      -4  /* workspace missing or too small */
+#define TASFT_ERR_TOO_LARGE      -5  /* a size exceeds a fixed capacity */
+
+/* device error word bits (OR-ed into *err when err != NULL) */
+#define TASFT_DEVERR_INDEX        1  /* a kept index outside [0, NB_k) was skipped */
+#define TASFT_DEVERR_TIMEOUT      2  /* a bounded wait gave up */
+#define TASFT_DEVERR_ORDER        4  /* a kept list was not strictly ascending */
+
+/* element types */
+#define TASFT_F32   0
+#define TASFT_BF16  1
+#define TASFT_F16   2
+
+typedef void* tasft_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+/* ------------------------------------------------------------------------- */
+/* AttnGate: pooled pair-MLP scores, hard mask and kept-block lists          */
+/* ------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;          /* [B, Hq, Sq, D]  dtype */
+  const void* k;          /* [B, Hk, Sk, D]  dtype, Hq % Hk == 0 (GQA: K shared per group) */
+  int64_t q_stride[4];
+  int64_t k_stride[4];
+  int32_t B, Hq, Hk, Sq, Sk, D;
+  int32_t block;          /* tokens per block (any positive value) */
+  int32_t dtype;          /* TASFT_F32 / TASFT_BF16 / TASFT_F16 */
+  int32_t hidden;         /* gate MLP width, <= 256 */
+  const float* w_in;      /* [hidden, 2D] fp32 row-major (nn.Linear weight) */
+  const float* b_in;      /* [hidden] fp32 */
+  const float* w_out;     /* [hidden] fp32 */
+  int32_t causal;         /* zero blocks j > i when NB_q == NB_k (reference semantics) */
+  float tau;              /* hard = soft >= tau */
+  float* soft;            /* out [B, Hq, NBq, NBk] fp32 (required) */
+  uint8_t* hard;          /* out [B, Hq, NBq, NBk] bool, or NULL */
+  int32_t* kept_idx;      /* out [B, Hq, NBq, NBk] ascending kept k-blocks, -1 padded, or NULL */
+  int32_t* kept_cnt;      /* out [B, Hq, NBq], or NULL (required with kept_idx) */
+  int32_t* num_kept;      /* out scalar: total kept blocks over the full grid, or NULL */
+  float* pooled_q;        /* out [B, Hq, NBq, D] fp32 block means, or NULL */
+  float* pooled_k;        /* out [B, Hk, NBk, D] fp32 block means, or NULL */
+  void* workspace;        /* tasft_gate_workspace_size() bytes */
+  int64_t workspace_bytes;
+} tasft_gate_args;
+
+TASFT_API int64_t tasft_gate_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t Sq, int32_t Sk,
+                                  int32_t block, int32_t hidden);
+TASFT_API int tasft_gate_mask_build(const tasft_gate_args* args, tasft_stream_t stream);
+
+/* Threshold given fp32 scores: hard = (soft >= tau) (& block tril when causal),
+ * ascending kept lists, counts and the total. Bit-exact with the reference's
+ * `soft >= tau` on the same scores. */
+typedef struct {
+  const float* soft;      /* [rows, NBk] fp32, rows = B*H*NBq, row-major */
+  int64_t rows;
+  int32_t NBq, NBk;       /* row r is q-block (r % NBq) */
+  int32_t causal;         /* also drop k-block > q-block */
+  float tau;
+  uint8_t* hard;          /* out [rows, NBk] or NULL */
+  int32_t* kept_idx;      /* out [rows, NBk] -1 padded, or NULL */
+  int32_t* kept_cnt;      /* out [rows] or NULL */
+  int32_t* num_kept;      /* out scalar or NULL */
+} tasft_threshold_args;
+TASFT_API int tasft_mask_from_scores(const tasft_threshold_args* args, tasft_stream_t stream);
+
+/* Bool block mask -> ascending kept lists (the reference kernel's visiting order). */
+typedef struct {
+  const uint8_t* mask;    /* [rows, NBk] bool, row-major */
+  int64_t rows;
+  int32_t NBq, NBk;
+  int32_t causal;         /* AND with the block lower triangle, as the reference host does */
+  int32_t* kept_idx;      /* out [rows, NBk] -1 padded */
+  int32_t* kept_cnt;      /* out [rows] */
+  int32_t* num_kept;      /* out scalar or NULL */
+} tasft_mask_args;
+TASFT_API int tasft_mask_to_kept(const tasft_mask_args* args, tasft_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Block-sparse prefill attention                                            */
+/* ------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;          /* [B, Hq, S, D] */
+  const void* k;          /* [B, Hk, S, D], Hq % Hk == 0 */
+  const void* v;          /* [B, Hk, S, D] */
+  void* out;              /* [B, Hq, S, D] */
+  int64_t q_stride[4], k_stride[4], v_stride[4], o_stride[4];
+  int32_t B, Hq, Hk, S, D;
+  int32_t block;          /* 32, 64 or 128 */
+  int32_t dtype;
+  int32_t causal;
+  float scale;            /* softmax scale, normally 1/sqrt(D) */
+  const int32_t* kept_idx;/* [B, Hm, NB, NB] ascending kept k-blocks per (b, head, q-block) */
+  const int32_t* kept_cnt;/* [B, Hm, NB] */
+  int32_t Hm;             /* heads of the lists: Hq (per q-head) or Hk (per kv-head) */
+  int32_t* err;           /* optional device error word */
+  int32_t force_simt;     /* 1 = use the CUDA-core kernel even where tcgen05 applies (testing) */
+} tasft_prefill_args;
+TASFT_API int tasft_bsa_prefill_fwd(const tasft_prefill_args* args, tasft_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Block-sparse decode (one query token per sequence), split-KV               */
+/* ------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;          /* [B, Hq, D] */
+  const void* k_cache;    /* [B, Hk, L, D] */
+  const void* v_cache;    /* [B, Hk, L, D] */
+  void* out;              /* [B, Hq, D] (may be NULL when only partials are wanted) */
+  int64_t q_stride[3], k_stride[4], v_stride[4], o_stride[3];
+  int32_t B, Hq, Hk, L, D;
+  int32_t block;
+  int32_t dtype;
+  float scale;
+  const int32_t* kv_len;  /* [B] valid cache length per sequence (<= L) */
+  const int32_t* kept_idx;/* [B, Hk, NBmax] ascending kept blocks per (sequence, kv-head) */
+  const int32_t* kept_cnt;/* [B, Hk] */
+  int32_t nb_max;         /* row length of kept_idx */
+  int32_t num_splits;     /* 0 = choose; else CTAs per (sequence, kv-head) */
+  float* part_o;          /* optional out [B, Hq, D] fp32 normalised partial (for cross-GPU combine) */
+  float* part_ml;         /* optional out [B, Hq, 2] fp32 (m, l) in base-e units */
+  void* workspace;        /* tasft_decode_workspace_size() bytes, zero-filled before first use */
+  int64_t workspace_bytes;
+  int32_t* err;
+} tasft_decode_args;
+TASFT_API int64_t tasft_decode_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t D, int32_t max_splits);
+TASFT_API int tasft_bsa_decode_fwd(const tasft_decode_args* args, tasft_stream_t stream);
+
+/* Merge G partial results (normalised o, m, l) into the final output. */
+typedef struct {
+  const float* part_o;    /* [G, rows, D] fp32 */
+  const float* part_ml;   /* [G, rows, 2] fp32 */
+  int32_t G;
+  int64_t rows;           /* B * Hq */
+  int32_t D;
+  void* out;              /* [rows, D] contiguous, dtype */
+  int32_t dtype;
+} tasft_combine_args;
+TASFT_API int tasft_bsa_decode_combine(const tasft_combine_args* args, tasft_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Training-time gate target, losses and gate backward                       */
+/* ------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;          /* [B, Hq, S, D] */
+  const void* k;          /* [B, Hk, S, D] */
+  int64_t q_stride[4], k_stride[4];
+  int32_t B, Hq, Hk, S, D;
+  int32_t block;
+  int32_t dtype;
+  float scale;            /* 1/sqrt(D) */
+  int32_t emulate_bf16_scores; /* round block maxima as the reference's bf16 (QK^T)*scale */
+  float temperature;      /* 1 = compute_gate_target; 2 = the alternate target */
+  float clamp;            /* <= 0: none; else clamp finite maxima to [-clamp, clamp] */
+  float* block_max;       /* out [B, Hq, NB, NB] fp32 (upper triangle = -inf), or NULL */
+  float* target;          /* out [B, Hq, NB, NB] fp32 softmax over the NB*NB grid */
+  void* workspace;        /* tasft_gate_target_workspace_size() bytes */
+  int64_t workspace_bytes;
+  int32_t force_simt;
+  int32_t* err;
+} tasft_target_args;
+TASFT_API int64_t tasft_gate_target_workspace_size(int32_t B, int32_t Hq, int32_t S, int32_t block);
+TASFT_API int tasft_gate_target_fwd(const tasft_target_args* args, tasft_stream_t stream);
+
+typedef struct {
+  const float* soft;      /* [B, H, NB, NB] gate scores */
+  const float* target;    /* [B, H, NB, NB] */
+  int32_t B, H, NBq, NBk;
+  float tau_target;       /* sparsity target */
+  float w_kl, w_sparse;   /* d_soft = w_kl dKL/dsoft + w_sparse dSparse/dsoft */
+  float* kl;              /* out scalar: KL(target || gate), batchmean */
+  float* sparse;          /* out scalar: (mean(soft) - tau)^2 */
+  float* d_soft;          /* out [B, H, NB, NB] or NULL */
+  void* workspace;        /* tasft_gate_loss_workspace_size() bytes */
+  int64_t workspace_bytes;
+} tasft_loss_args;
+TASFT_API int64_t tasft_gate_loss_workspace_size(int32_t B, int32_t H);
+TASFT_API int tasft_gate_loss_fwd_bwd(const tasft_loss_args* args, tasft_stream_t stream);
+
+typedef struct {
+  const float* pooled_q;  /* [B, Hq, NBq, D] from tasft_gate_mask_build */
+  const float* pooled_k;  /* [B, Hk, NBk, D] */
+  const float* d_soft;    /* [B, Hq, NBq, NBk] upstream gradient of the soft scores */
+  const float* soft;      /* [B, Hq, NBq, NBk] the forward soft scores */
+  int32_t B, Hq, Hk, NBq, NBk, D, hidden;
+  int32_t causal;
+  const float* w_in;      /* [hidden, 2D] */
+  const float* b_in;      /* [hidden] */
+  const float* w_out;     /* [hidden] */
+  float* d_w_in;          /* out [hidden, 2D] (overwritten) */
+  float* d_b_in;          /* out [hidden] */
+  float* d_w_out;         /* out [hidden] */
+  float* d_pooled_q;      /* out [B, Hq, NBq, D] or NULL */
+  float* d_pooled_k;      /* out [B, Hk, NBk, D] or NULL */
+  void* workspace;        /* tasft_gate_bwd_workspace_size() bytes */
+  int64_t workspace_bytes;
+} tasft_gate_bwd_args;
+TASFT_API int64_t tasft_gate_bwd_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t NBq, int32_t NBk,
+                                      int32_t hidden);
+TASFT_API int tasft_gate_bwd(const tasft_gate_bwd_args* args, tasft_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Misc                                                                      */
+/* ------------------------------------------------------------------------- */
+TASFT_API const char* tasft_status_string(int status);
+TASFT_API int tasft_abi_version(void);
+/* Number of kernels this library launched since load (for launch accounting). */
+TASFT_API int64_t tasft_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TASFT_B200_H_ */

@@ -1,0 +1,223 @@
+"""Drop-in ``AttnGate`` whose forward is the fused sm_100a mask builder.
+
+Mirrors ``tasft/modules/attn_gate.py``: same constructor and validation (:271-338), the
+same parameters ``gate_proj_in.{weight,bias}`` / ``gate_proj_out.weight`` and init
+(:340-349) so bundle state dicts load unchanged, and ``forward(q, k, threshold)``
+returning :class:`GateOutput` (:230-246, :377-485). Additions: K may carry the kv-heads
+of a GQA group (no ``repeat_interleave``), ``Sq`` may differ from ``Sk`` (decode
+scoring), and the output also carries the kept-block lists. Scores are fp32. The
+sparsity ratio is read from the device lazily, on first access.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+
+from tasft_b200 import _lib as L
+from tasft_b200.exceptions import ValidationError
+from tasft_b200.types import KeptBlocks
+
+
+@dataclass(frozen=True)
+class GateOutput:
+    """Result of :meth:`AttnGate.forward` (fields of ``tasft/modules/attn_gate.py:230-246``)."""
+
+    soft_scores: torch.Tensor
+    hard_mask: torch.Tensor
+    num_blocks_q: int
+    num_blocks_k: int
+    kept: KeptBlocks | None = None
+    _num_kept: torch.Tensor | None = field(default=None, repr=False)
+    _ratio: list = field(default_factory=list, repr=False)
+
+    @property
+    def sparsity_ratio(self) -> float:
+        """``1 - mean(hard_mask)`` over the full grid (host sync on first access)."""
+        if not self._ratio:
+            total = self.hard_mask.numel()
+            kept = int(self._num_kept.item()) if self._num_kept is not None else int(self.hard_mask.sum().item())
+            self._ratio.append(1.0 - kept / max(total, 1))
+        return self._ratio[0]
+
+
+class _GateFn(torch.autograd.Function):
+    """Soft scores with a CUDA backward to the gate parameters and to q/k."""
+
+    @staticmethod
+    def forward(ctx, q, k, w_in, b_in, w_out, gate, tau):  # noqa: D401
+        res = gate._launch(q, k, tau, want_pooled=True)
+        ctx.save_for_backward(res["pooled_q"], res["pooled_k"], res["soft"], w_in, b_in, w_out)
+        ctx.meta = (q.shape, k.shape, q.dtype, gate.block_size, gate.is_causal)
+        ctx.mark_non_differentiable(res["hard"])
+        return res["soft"], res["hard"], res["kept_idx"], res["kept_cnt"], res["num_kept"]
+
+    @staticmethod
+    def backward(ctx, d_soft, *_):
+        from tasft_b200.training import gate_backward  # noqa: PLC0415
+
+        pq, pk, soft, w_in, b_in, w_out = ctx.saved_tensors
+        qshape, kshape, qdtype, block, causal = ctx.meta
+        g = gate_backward(pq, pk, soft, d_soft.contiguous().float(), w_in, b_in, w_out, causal,
+                          need_inputs=ctx.needs_input_grad[0] or ctx.needs_input_grad[1])
+        dq = dk = None
+        if ctx.needs_input_grad[0]:
+            dq = _unpool(g["d_pooled_q"], qshape, block).to(qdtype)
+        if ctx.needs_input_grad[1]:
+            dk = _unpool(g["d_pooled_k"], kshape, block).to(qdtype)
+        return dq, dk, g["d_w_in"], g["d_b_in"], g["d_w_out"].view(1, -1), None, None
+
+
+def _unpool(d_pooled: torch.Tensor, shape, block: int) -> torch.Tensor:
+    """Gradient of the zero-padded block mean: every token of block i gets d_i / block."""
+    b, h, s, d = shape
+    rep = (d_pooled / block).repeat_interleave(block, dim=2)
+    return rep[:, :, :s, :]
+
+
+class AttnGate(nn.Module):
+    """Learnable block-importance predictor (see ``tasft/modules/attn_gate.py:249-338``)."""
+
+    def __init__(
+        self,
+        num_heads: int,
+        head_dim: int,
+        block_size: int = 64,
+        gate_hidden_dim: int | None = None,
+        default_threshold: float = 0.5,
+        is_causal: bool = True,
+    ) -> None:
+        super().__init__()
+        if num_heads <= 0:
+            raise ValidationError(f"num_heads must be positive, got {num_heads}", context={"num_heads": num_heads})
+        if head_dim <= 0:
+            raise ValidationError(f"head_dim must be positive, got {head_dim}", context={"head_dim": head_dim})
+        if block_size <= 0:
+            raise ValidationError(f"block_size must be positive, got {block_size}", context={"block_size": block_size})
+        if not 0.0 <= default_threshold <= 1.0:
+            raise ValidationError(f"default_threshold must be in [0, 1], got {default_threshold}",
+                                  context={"default_threshold": default_threshold})
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.block_size = block_size
+        self.default_threshold = default_threshold
+        self.is_causal = is_causal
+        hid = gate_hidden_dim if gate_hidden_dim is not None else max(32, head_dim // 4)
+        self.gate_hidden_dim = hid
+        self.gate_proj_in = nn.Linear(2 * head_dim, hid, bias=True)
+        self.gate_proj_out = nn.Linear(hid, 1, bias=False)
+        self._init_weights()
+
+    def _init_weights(self) -> None:
+        nn.init.xavier_uniform_(self.gate_proj_in.weight)
+        nn.init.zeros_(self.gate_proj_in.bias)
+        nn.init.normal_(self.gate_proj_out.weight, std=0.01)
+
+    # ------------------------------------------------------------------
+    def _validate(self, q: torch.Tensor, k: torch.Tensor) -> None:
+        if q.ndim != 4:
+            raise ValidationError(f"Expected 4D Q tensor [B, H, S, D], got ndim={q.ndim}",
+                                  context={"q_shape": list(q.shape)})
+        if k.ndim != 4:
+            raise ValidationError(f"Expected 4D K tensor [B, H, S, D], got ndim={k.ndim}",
+                                  context={"k_shape": list(k.shape)})
+        B, H, S, D = q.shape
+        if k.shape[0] != B or k.shape[3] != D or k.shape[1] <= 0 or H % k.shape[1] != 0:
+            raise ValidationError(f"Q and K must have same shape, got {q.shape} vs {k.shape}",
+                                  context={"q_shape": list(q.shape), "k_shape": list(k.shape)})
+        if self.num_heads != H:
+            raise ValidationError(f"Expected {self.num_heads} heads, got {H}",
+                                  context={"expected_heads": self.num_heads, "actual_heads": H})
+        if self.head_dim != D:
+            raise ValidationError(f"Expected head_dim={self.head_dim}, got {D}",
+                                  context={"expected_dim": self.head_dim, "actual_dim": D})
+        if S == 0 or k.shape[2] == 0:
+            raise ValidationError("Sequence length must be > 0", context={"seq_len": S})
+        L.require_cuda(q, k)
+
+    def _launch(self, q: torch.Tensor, k: torch.Tensor, tau: float, want_pooled: bool = False,
+                want_lists: bool = True) -> dict:
+        q = q.detach().contiguous()
+        k = k.detach().contiguous()
+        B, Hq, Sq, D = q.shape
+        Hk, Sk = k.shape[1], k.shape[2]
+        blk = self.block_size
+        nbq, nbk = math.ceil(Sq / blk), math.ceil(Sk / blk)
+        dev = q.device
+        hid = self.gate_hidden_dim
+        w_in = self.gate_proj_in.weight.detach().float().contiguous()
+        b_in = self.gate_proj_in.bias.detach().float().contiguous()
+        w_out = self.gate_proj_out.weight.detach().float().contiguous().view(-1)
+        soft = torch.empty(B, Hq, nbq, nbk, dtype=torch.float32, device=dev)
+        hard = torch.empty(B, Hq, nbq, nbk, dtype=torch.bool, device=dev)
+        idx = torch.empty(B, Hq, nbq, nbk, dtype=torch.int32, device=dev) if want_lists else None
+        cnt = torch.empty(B, Hq, nbq, dtype=torch.int32, device=dev) if want_lists else None
+        num = torch.zeros(1, dtype=torch.int32, device=dev)
+        pq = torch.empty(B, Hq, nbq, D, dtype=torch.float32, device=dev) if want_pooled else None
+        pk = torch.empty(B, Hk, nbk, D, dtype=torch.float32, device=dev) if want_pooled else None
+        lib = L.lib()
+        ws_bytes = lib.tasft_gate_workspace_size(B, Hq, Hk, Sq, Sk, blk, hid)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        args = L.GateArgs(
+            q=q.data_ptr(), k=k.data_ptr(), q_stride=L.strides4(q), k_stride=L.strides4(k),
+            B=B, Hq=Hq, Hk=Hk, Sq=Sq, Sk=Sk, D=D, block=blk, dtype=L.dtype_code(q), hidden=hid,
+            w_in=w_in.data_ptr(), b_in=b_in.data_ptr(), w_out=w_out.data_ptr(),
+            causal=int(self.is_causal), tau=float(tau), soft=soft.data_ptr(), hard=hard.data_ptr(),
+            kept_idx=L.ptr(idx), kept_cnt=L.ptr(cnt), num_kept=num.data_ptr(),
+            pooled_q=L.ptr(pq), pooled_k=L.ptr(pk), workspace=ws.data_ptr(), workspace_bytes=ws_bytes,
+        )
+        L.check(lib.tasft_gate_mask_build(args, L.stream_ptr(dev)), "tasft_gate_mask_build",
+                shape=[B, Hq, Hk, Sq, Sk, D])
+        return {"soft": soft, "hard": hard, "kept_idx": idx, "kept_cnt": cnt, "num_kept": num,
+                "pooled_q": pq, "pooled_k": pk, "nbq": nbq, "nbk": nbk}
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, threshold: float | None = None) -> GateOutput:
+        tau = threshold if threshold is not None else self.default_threshold
+        self._validate(q, k)
+        params = (self.gate_proj_in.weight, self.gate_proj_in.bias, self.gate_proj_out.weight)
+        needs_grad = torch.is_grad_enabled() and (
+            q.requires_grad or k.requires_grad or any(p.requires_grad for p in params))
+        if needs_grad:
+            soft, hard, idx, cnt, num = _GateFn.apply(q, k, *params, self, tau)
+            nbq, nbk = soft.shape[2], soft.shape[3]
+        else:
+            r = self._launch(q, k, tau)
+            soft, hard, idx, cnt, num, nbq, nbk = (r["soft"], r["hard"], r["kept_idx"], r["kept_cnt"],
+                                                   r["num_kept"], r["nbq"], r["nbk"])
+        return GateOutput(soft_scores=soft, hard_mask=hard, num_blocks_q=nbq, num_blocks_k=nbk,
+                          kept=KeptBlocks(idx, cnt), _num_kept=num)
+
+    def compute_sparsity(self, soft_scores: torch.Tensor, threshold: float) -> float:
+        """``1 - mean(soft >= tau)`` (attn_gate.py:487-497)."""
+        return 1.0 - (soft_scores >= threshold).float().mean().item()
+
+    @property
+    def num_parameters(self) -> int:
+        return sum(p.numel() for p in self.parameters() if p.requires_grad)
+
+    def extra_repr(self) -> str:
+        return (f"num_heads={self.num_heads}, head_dim={self.head_dim}, block_size={self.block_size}, "
+                f"gate_hidden_dim={self.gate_hidden_dim}, default_threshold={self.default_threshold}, "
+                f"is_causal={self.is_causal}, params={self.num_parameters}")
+
+
+def threshold_scores(soft: torch.Tensor, tau: float, causal: bool) -> tuple[torch.Tensor, KeptBlocks, torch.Tensor]:
+    """Hard mask and kept lists from given fp32 scores (bit-exact ``soft >= tau``)."""
+    L.require_cuda(soft)
+    s = soft.float().contiguous()
+    nbq, nbk = s.shape[-2], s.shape[-1]
+    rows = s.numel() // nbk
+    hard = torch.empty(s.shape, dtype=torch.bool, device=s.device)
+    idx = torch.empty(s.shape, dtype=torch.int32, device=s.device)
+    cnt = torch.empty(s.shape[:-1], dtype=torch.int32, device=s.device)
+    num = torch.zeros(1, dtype=torch.int32, device=s.device)
+    args = L.ThresholdArgs(soft=s.data_ptr(), rows=rows, NBq=nbq, NBk=nbk, causal=int(causal), tau=float(tau),
+                           hard=hard.data_ptr(), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(),
+                           num_kept=num.data_ptr())
+    L.check(L.lib().tasft_mask_from_scores(args, L.stream_ptr(s.device)), "tasft_mask_from_scores")
+    return hard, KeptBlocks(idx, cnt), num
+
+
+__all__ = ["AttnGate", "GateOutput", "threshold_scores"]

@@ -1,0 +1,431 @@
+// Training-time gate target, gate losses and the gate backward.
+//
+// Reference path (tasft/modules/tasft_attention.py:427-458 -> tasft/training/objectives.py):
+//   scores = (Q K^T) * scale (+ causal -inf), 2-D max-pool over 64x64 tiles
+//   (objectives.py:170-178), softmax over the flattened NB x NB grid (:180-185),
+//   KL(target || soft / sum soft) batchmean (:187-221), (mean(soft) - tau)^2 (:223-241).
+// Here the S x S score matrix is never stored: each tile's max is reduced on chip.
+#include "common.cuh"
+
+namespace tasft {
+
+int gate_target_blockmax_tc(const tasft_target_args& a, float* block_max, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// CUDA-core tile max: one CTA per (q-block, k-block <= q-block, b*h).
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(256) blockmax_simt_kernel(tasft_target_args a, float* bm, int NB) {
+  const int qb = blockIdx.x, kb = blockIdx.y, bh = blockIdx.z;
+  const int b = bh / a.Hq, hq = bh % a.Hq;
+  const int blk = a.block;
+  float* dst = bm + ((int64_t)bh * NB + qb) * NB + kb;
+  if (kb > qb) {
+    if (threadIdx.x == 0) *dst = -INFINITY;
+    return;
+  }
+  extern __shared__ float sm[];
+  float* Qs = sm;                  // [blk][D+1]
+  float* Ks = sm + blk * (D + 1);  // [blk][D+1]
+  const int hk = hq / (a.Hq / a.Hk);
+  const T* Q = reinterpret_cast<const T*>(a.q) + b * a.q_stride[0] + hq * a.q_stride[1];
+  const T* K = reinterpret_cast<const T*>(a.k) + b * a.k_stride[0] + hk * a.k_stride[1];
+  for (int x = threadIdx.x; x < blk * D; x += blockDim.x) {
+    const int r = x / D, d = x % D;
+    const int qp = qb * blk + r, kp = kb * blk + r;
+    Qs[r * (D + 1) + d] = qp < a.S ? to_f<T>(Q[(int64_t)qp * a.q_stride[2] + d]) : 0.f;
+    Ks[r * (D + 1) + d] = kp < a.S ? to_f<T>(K[(int64_t)kp * a.k_stride[2] + d]) : 0.f;
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int e = threadIdx.x; e < blk * blk; e += blockDim.x) {
+    const int r = e / blk, c = e % blk;
+    const int qp = qb * blk + r, kp = kb * blk + c;
+    if (qp >= a.S || kp >= a.S || kp > qp) continue;
+    float s = 0.f;
+#pragma unroll 8
+    for (int d = 0; d < D; ++d) s = fmaf(Qs[r * (D + 1) + d], Ks[c * (D + 1) + d], s);
+    mx = fmaxf(mx, s);
+  }
+  mx = warp_max(mx);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+    float v;
+    if (a.emulate_bf16_scores) {
+      // reference: bf16(bf16(q.k) * scale); both roundings are monotone, so max commutes
+      v = __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(m)) * a.scale));
+    } else {
+      v = m * a.scale;
+    }
+    *dst = v;
+  }
+}
+
+// Softmax over each (b, h) grid of NB*NB block maxima (objectives.py:180-185), with the
+// alternate target's clamp and temperature (tasft_attention.py:278-289) as options.
+__global__ void target_softmax_kernel(const float* bm, float* target, int64_t n, float inv_temp, float clamp) {
+  const int64_t base = (int64_t)blockIdx.x * n;
+  __shared__ float red[32];
+  auto val = [&](int64_t i) {
+    float x = bm[base + i];
+    if (clamp > 0.f && isfinite(x)) x = fminf(fmaxf(x, -clamp), clamp);
+    return x * inv_temp;
+  };
+  float mx = -INFINITY;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) mx = fmaxf(mx, val(i));
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -INFINITY;
+    m = warp_max(m);
+    if (threadIdx.x == 0) red[0] = m;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += __expf(val(i) - mx);
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = 1.0f / red[0];
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) target[base + i] = __expf(val(i) - mx) * inv;
+}
+
+// ---------------------------------------------------------------------------
+// Loss forward + gradient w.r.t. the soft scores.
+// ---------------------------------------------------------------------------
+constexpr float kEps = 1e-8f;
+
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+  return t;
+}
+
+// one CTA per (b, h): partial KL, partial sum, and w_kl * dKL/dsoft
+__global__ void loss_rows_kernel(tasft_loss_args a, double* part) {
+  const int64_t n = (int64_t)a.NBq * a.NBk;
+  const int64_t base = (int64_t)blockIdx.x * n;
+  __shared__ double red[32];
+  double s = 0.0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += a.soft[base + i];
+  const double S = block_sum_d(s, red);
+  const float denom = (float)S + kEps;
+  double kl = 0.0, cross = 0.0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float t = a.target[base + i];
+    const float g = a.soft[base + i] / denom;
+    if (t > 0.f) kl += (double)t * ((double)logf(t) - (double)logf(g + kEps));
+    cross += (double)t * a.soft[base + i] / (g + kEps);
+  }
+  const double KL = block_sum_d(kl, red);
+  const double X = block_sum_d(cross, red);
+  if (a.d_soft) {
+    const float invB = 1.0f / (float)a.B;
+    const float c2 = (float)(X / ((double)denom * denom));
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+      const float t = a.target[base + i];
+      const float g = a.soft[base + i] / denom;
+      const float d = -invB * (t / ((g + kEps) * denom) - c2);
+      a.d_soft[base + i] = a.w_kl * d;
+    }
+  }
+  if (threadIdx.x == 0) {
+    part[2 * blockIdx.x] = KL;
+    part[2 * blockIdx.x + 1] = S;
+  }
+}
+
+__global__ void loss_final_kernel(tasft_loss_args a, const double* part, int rows, float* gsp) {
+  __shared__ double red[32];
+  double kl = 0.0, s = 0.0;
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+    kl += part[2 * i];
+    s += part[2 * i + 1];
+  }
+  const double KL = block_sum_d(kl, red);
+  const double Ssum = block_sum_d(s, red);
+  if (threadIdx.x == 0) {
+    const double N = (double)a.B * a.H * a.NBq * a.NBk;
+    const double mean = Ssum / N;
+    const double dev = mean - (double)a.tau_target;
+    if (a.kl) *a.kl = (float)(KL / a.B);
+    if (a.sparse) *a.sparse = (float)(dev * dev);
+    *gsp = (float)(a.w_sparse * 2.0 * dev / N);
+  }
+}
+
+__global__ void loss_add_kernel(float* d, int64_t n, const float* gsp) {
+  const float g = *gsp;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    d[i] += g;
+}
+
+// ---------------------------------------------------------------------------
+// Gate backward: soft = sigmoid(w_out . relu(a_i + c_j)) (zeroed above the diagonal)
+// ---------------------------------------------------------------------------
+// A [rows_q, hid] = W_q pq + b ; Ct [B*Hk, hid, NBk] = W_k pk
+__global__ void bwd_project_kernel(tasft_gate_bwd_args a, float* A, float* Ct) {
+  const int64_t rq = (int64_t)a.B * a.Hq * a.NBq;
+  int64_t r = blockIdx.x;
+  const bool isq = r < rq;
+  if (!isq) r -= rq;
+  const float* x = (isq ? a.pooled_q : a.pooled_k) + r * a.D;
+  const int off = isq ? 0 : a.D;
+  for (int h = threadIdx.x; h < a.hidden; h += blockDim.x) {
+    const float* w = a.w_in + (int64_t)h * 2 * a.D + off;
+    float s = 0.f;
+    for (int d = 0; d < a.D; ++d) s = fmaf(w[d], x[d], s);
+    if (isq) A[r * a.hidden + h] = s + a.b_in[h];
+    else {
+      const int64_t bh = r / a.NBk, j = r % a.NBk;
+      Ct[(bh * a.hidden + h) * a.NBk + j] = s;
+    }
+  }
+}
+
+__device__ __forceinline__ float dlogit_of(const tasft_gate_bwd_args& a, int64_t idx) {
+  const float s = a.soft[idx];
+  return a.d_soft[idx] * s * (1.f - s);
+}
+
+// rows: one warp per (b, hq, i); dA[row][h], dwo[row][h]
+__global__ void bwd_rows_kernel(tasft_gate_bwd_args a, const float* A, const float* Ct, float* dA, float* dwo) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  const int64_t rows = (int64_t)a.B * a.Hq * a.NBq;
+  if (row >= rows) return;
+  const int hq = (int)((row / a.NBq) % a.Hq), b = (int)(row / ((int64_t)a.NBq * a.Hq));
+  const int hk = hq / (a.Hq / a.Hk);
+  const float* ct = Ct + ((int64_t)b * a.Hk + hk) * a.hidden * a.NBk;
+  for (int h = 0; h < a.hidden; ++h) {
+    const float ai = A[row * a.hidden + h];
+    const float wh = a.w_out[h];
+    float da = 0.f, dw = 0.f;
+    for (int j = lane; j < a.NBk; j += 32) {
+      const float dl = dlogit_of(a, row * a.NBk + j);
+      const float pre = ai + ct[(int64_t)h * a.NBk + j];
+      if (pre > 0.f) {
+        da = fmaf(dl, wh, da);
+        dw = fmaf(dl, pre, dw);
+      }
+    }
+    da = warp_sum(da);
+    dw = warp_sum(dw);
+    if (lane == 0) {
+      dA[row * a.hidden + h] = da;
+      dwo[row * a.hidden + h] = dw;
+    }
+  }
+}
+
+// cols: one warp per (b, hk, j); dC[col][h] summed over the group's q-heads and rows
+__global__ void bwd_cols_kernel(tasft_gate_bwd_args a, const float* A, const float* Ct, float* dC) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t col = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  const int64_t cols = (int64_t)a.B * a.Hk * a.NBk;
+  if (col >= cols) return;
+  const int j = (int)(col % a.NBk);
+  const int64_t bhk = col / a.NBk;
+  const int hk = (int)(bhk % a.Hk), b = (int)(bhk / a.Hk);
+  const int grp = a.Hq / a.Hk;
+  const int rows = grp * a.NBq;
+  for (int h = 0; h < a.hidden; ++h) {
+    const float cj = Ct[(bhk * a.hidden + h) * a.NBk + j];
+    const float wh = a.w_out[h];
+    float dc = 0.f;
+    for (int t = lane; t < rows; t += 32) {
+      const int g = t / a.NBq, i = t % a.NBq;
+      const int64_t row = ((int64_t)b * a.Hq + hk * grp + g) * a.NBq + i;
+      const float pre = A[row * a.hidden + h] + cj;
+      if (pre > 0.f) dc = fmaf(dlogit_of(a, row * a.NBk + j), wh, dc);
+    }
+    dc = warp_sum(dc);
+    if (lane == 0) dC[col * a.hidden + h] = dc;
+  }
+}
+
+// weight grads: CTA per (h, half); threads over d. half 0: rows/pq, half 1: cols/pk
+__global__ void bwd_weights_kernel(tasft_gate_bwd_args a, const float* dA, const float* dwo, const float* dC) {
+  const int h = blockIdx.x, half = blockIdx.y;
+  const int64_t n = half == 0 ? (int64_t)a.B * a.Hq * a.NBq : (int64_t)a.B * a.Hk * a.NBk;
+  const float* g = half == 0 ? dA : dC;
+  const float* x = half == 0 ? a.pooled_q : a.pooled_k;
+  for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+    float s = 0.f;
+    for (int64_t r = 0; r < n; ++r) s = fmaf(g[r * a.hidden + h], x[r * a.D + d], s);
+    a.d_w_in[(int64_t)h * 2 * a.D + half * a.D + d] = s;
+  }
+  if (half == 0 && threadIdx.x < 32) {
+    float sb = 0.f, sw = 0.f;
+    for (int64_t r = threadIdx.x; r < n; r += 32) {
+      sb += dA[r * a.hidden + h];
+      sw += dwo[r * a.hidden + h];
+    }
+    sb = warp_sum(sb);
+    sw = warp_sum(sw);
+    if (threadIdx.x == 0) {
+      a.d_b_in[h] = sb;
+      a.d_w_out[h] = sw;
+    }
+  }
+}
+
+// input grads: d_pooled[r][d] = sum_h g[r][h] W[h][off + d]
+__global__ void bwd_inputs_kernel(tasft_gate_bwd_args a, const float* dA, const float* dC) {
+  const int64_t rq = (int64_t)a.B * a.Hq * a.NBq;
+  int64_t r = blockIdx.x;
+  const bool isq = r < rq;
+  if (!isq) r -= rq;
+  float* out = isq ? a.d_pooled_q : a.d_pooled_k;
+  if (!out) return;
+  const float* g = (isq ? dA : dC) + r * a.hidden;
+  const int off = isq ? 0 : a.D;
+  for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+    float s = 0.f;
+    for (int h = 0; h < a.hidden; ++h) s = fmaf(g[h], a.w_in[(int64_t)h * 2 * a.D + off + d], s);
+    out[r * a.D + d] = s;
+  }
+}
+
+template <typename T, int D>
+static int launch_bm_simt(const tasft_target_args& a, float* bm, int NB, cudaStream_t st) {
+  const size_t smem = (size_t)2 * a.block * (D + 1) * sizeof(float);
+  auto kern = blockmax_simt_kernel<T, D>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return TASFT_ERR_CUDA;
+  dim3 grid(NB, NB, a.B * a.Hq);
+  kern<<<grid, 256, smem, st>>>(a, bm, NB);
+  count_launch();
+  return launch_status();
+}
+
+template <typename T>
+static int launch_bm_simt_dt(const tasft_target_args& a, float* bm, int NB, cudaStream_t st) {
+  switch (a.D) {
+    case 32: return launch_bm_simt<T, 32>(a, bm, NB, st);
+    case 64: return launch_bm_simt<T, 64>(a, bm, NB, st);
+    case 128: return launch_bm_simt<T, 128>(a, bm, NB, st);
+    default: return TASFT_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace tasft
+
+using namespace tasft;
+
+extern "C" int64_t tasft_gate_target_workspace_size(int32_t B, int32_t Hq, int32_t S, int32_t block) {
+  if (B <= 0 || Hq <= 0 || S <= 0 || block <= 0) return -1;
+  const int64_t NB = ceil_div(S, block);
+  return ((int64_t)B * Hq * NB * NB * 4 + 255) / 256 * 256;
+}
+
+extern "C" int tasft_gate_target_fwd(const tasft_target_args* ap, tasft_stream_t stream) {
+  if (!ap) return TASFT_ERR_INVALID_ARG;
+  const tasft_target_args& a = *ap;
+  if (!a.q || !a.k || !a.target) return TASFT_ERR_INVALID_ARG;
+  if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.S <= 0 || a.D <= 0 || a.block <= 0 || a.Hq % a.Hk)
+    return TASFT_ERR_INVALID_ARG;
+  if (a.q_stride[3] != 1 || a.k_stride[3] != 1) return TASFT_ERR_INVALID_ARG;
+  if (a.block > 128) return TASFT_ERR_UNSUPPORTED;
+  const int NB = ceil_div(a.S, a.block);
+  float* bm = a.block_max;
+  if (!bm) {
+    if (!a.workspace || a.workspace_bytes < tasft_gate_target_workspace_size(a.B, a.Hq, a.S, a.block))
+      return TASFT_ERR_WORKSPACE;
+    bm = reinterpret_cast<float*>(a.workspace);
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc = TASFT_ERR_UNSUPPORTED;
+  if (!a.force_simt) rc = gate_target_blockmax_tc(a, bm, st);
+  if (rc == TASFT_ERR_UNSUPPORTED) {
+    switch (a.dtype) {
+      case TASFT_F32: rc = launch_bm_simt_dt<float>(a, bm, NB, st); break;
+      case TASFT_BF16: rc = launch_bm_simt_dt<__nv_bfloat16>(a, bm, NB, st); break;
+      case TASFT_F16: rc = launch_bm_simt_dt<__half>(a, bm, NB, st); break;
+      default: return TASFT_ERR_UNSUPPORTED;
+    }
+  }
+  if (rc != TASFT_OK) return rc;
+  const float inv_t = a.temperature > 0.f ? 1.0f / a.temperature : 1.0f;
+  target_softmax_kernel<<<a.B * a.Hq, 512, 0, st>>>(bm, a.target, (int64_t)NB * NB, inv_t, a.clamp);
+  count_launch();
+  return launch_status();
+}
+
+extern "C" int64_t tasft_gate_loss_workspace_size(int32_t B, int32_t H) {
+  if (B <= 0 || H <= 0) return -1;
+  return ((int64_t)B * H * 16 + 256 + 255) / 256 * 256;
+}
+
+extern "C" int tasft_gate_loss_fwd_bwd(const tasft_loss_args* ap, tasft_stream_t stream) {
+  if (!ap) return TASFT_ERR_INVALID_ARG;
+  const tasft_loss_args& a = *ap;
+  if (!a.soft || !a.target || a.B <= 0 || a.H <= 0 || a.NBq <= 0 || a.NBk <= 0) return TASFT_ERR_INVALID_ARG;
+  if (!a.workspace || a.workspace_bytes < tasft_gate_loss_workspace_size(a.B, a.H)) return TASFT_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  double* part = reinterpret_cast<double*>(a.workspace);
+  float* gsp = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + (int64_t)a.B * a.H * 16);
+  const int rows = a.B * a.H;
+  loss_rows_kernel<<<rows, 256, 0, st>>>(a, part);
+  loss_final_kernel<<<1, 256, 0, st>>>(a, part, rows, gsp);
+  count_launch(2);
+  if (a.d_soft) {
+    const int64_t n = (int64_t)rows * a.NBq * a.NBk;
+    loss_add_kernel<<<ceil_div(n, 256) > 4096 ? 4096 : ceil_div(n, 256), 256, 0, st>>>(a.d_soft, n, gsp);
+    count_launch();
+  }
+  return launch_status();
+}
+
+extern "C" int64_t tasft_gate_bwd_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t NBq, int32_t NBk,
+                                                 int32_t hidden) {
+  if (B <= 0 || Hq <= 0 || Hk <= 0 || NBq <= 0 || NBk <= 0 || hidden <= 0) return -1;
+  const int64_t rq = (int64_t)B * Hq * NBq, rk = (int64_t)B * Hk * NBk;
+  const int64_t floats = rq * hidden * 3 + rk * hidden * 2;  // A, dA, dwo, Ct, dC
+  return (floats * 4 + 1023) / 256 * 256;
+}
+
+extern "C" int tasft_gate_bwd(const tasft_gate_bwd_args* ap, tasft_stream_t stream) {
+  if (!ap) return TASFT_ERR_INVALID_ARG;
+  const tasft_gate_bwd_args& a = *ap;
+  if (!a.pooled_q || !a.pooled_k || !a.d_soft || !a.soft || !a.w_in || !a.b_in || !a.w_out || !a.d_w_in ||
+      !a.d_b_in || !a.d_w_out)
+    return TASFT_ERR_INVALID_ARG;
+  if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.NBq <= 0 || a.NBk <= 0 || a.D <= 0 || a.hidden <= 0 || a.Hq % a.Hk)
+    return TASFT_ERR_INVALID_ARG;
+  const int64_t need = tasft_gate_bwd_workspace_size(a.B, a.Hq, a.Hk, a.NBq, a.NBk, a.hidden);
+  if (!a.workspace || a.workspace_bytes < need) return TASFT_ERR_WORKSPACE;
+  const int64_t rq = (int64_t)a.B * a.Hq * a.NBq, rk = (int64_t)a.B * a.Hk * a.NBk;
+  float* A = reinterpret_cast<float*>(a.workspace);
+  float* dA = A + rq * a.hidden;
+  float* dwo = dA + rq * a.hidden;
+  float* Ct = dwo + rq * a.hidden;
+  float* dC = Ct + rk * a.hidden;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  bwd_project_kernel<<<(unsigned)(rq + rk), 64, 0, st>>>(a, A, Ct);
+  bwd_rows_kernel<<<ceil_div(rq, 8), 256, 0, st>>>(a, A, Ct, dA, dwo);
+  bwd_cols_kernel<<<ceil_div(rk, 8), 256, 0, st>>>(a, A, Ct, dC);
+  bwd_weights_kernel<<<dim3(a.hidden, 2), 128, 0, st>>>(a, dA, dwo, dC);
+  bwd_inputs_kernel<<<(unsigned)(rq + rk), 128, 0, st>>>(a, dA, dC);
+  count_launch(5);
+  return launch_status();
+}

@@ -1,0 +1,107 @@
+"""Block-sparse decode (one query token per sequence) and the split-KV combine.
+
+New capability: the reference has no sparse decode (``tasft/inference/vllm_patch.py:189-196``
+hands decode to vLLM's dense forward). Queries of the q-heads of one GQA group attend
+over the kept KV blocks of their kv-head, bounded by ``kv_len``.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from tasft_b200 import _lib as L
+from tasft_b200.exceptions import KernelError
+from tasft_b200.types import KeptBlocks
+
+
+class DecodeWorkspace:
+    """Caller-owned split-KV scratch (partials + zeroed tickets), reused across calls."""
+
+    def __init__(self, B: int, Hq: int, Hk: int, D: int, max_splits: int, device) -> None:
+        self.max_splits = max_splits
+        self.bytes = int(L.lib().tasft_decode_workspace_size(B, Hq, Hk, D, max_splits))
+        self.buf = torch.zeros(self.bytes, dtype=torch.uint8, device=device)
+        self.key = (B, Hq, Hk, D)
+
+
+def default_splits(B: int, Hk: int, mean_kept: float, sms: int = 148) -> int:
+    """CTAs per (sequence, kv-head): enough to fill ~4 CTAs per SM, >= 2 blocks each."""
+    units = max(1, B * Hk)
+    want = math.ceil(4 * sms / units)
+    cap = max(1, int(mean_kept // 2))
+    return max(1, min(want, cap, 64))
+
+
+def bsa_decode(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    kv_len: torch.Tensor,
+    kept: KeptBlocks,
+    block: int = 64,
+    *,
+    num_splits: int = 0,
+    workspace: DecodeWorkspace | None = None,
+    out: torch.Tensor | None = None,
+    partials: tuple[torch.Tensor, torch.Tensor] | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor | None:
+    """Decode attention: q ``[B,Hq,D]``, caches ``[B,Hk,L,D]``, ``kv_len`` int32 ``[B]``,
+    ``kept`` lists ``[B,Hk,NBmax]`` / ``[B,Hk]``. Returns ``[B,Hq,D]`` (``out``) and, when
+    ``partials=(o [B,Hq,D] f32, ml [B,Hq,2] f32)`` is given, also writes the normalised
+    output with its (max, sum) for a cross-GPU combine."""
+    L.require_cuda(q, k_cache, v_cache, kv_len)
+    if q.ndim != 3 or k_cache.ndim != 4 or k_cache.shape != v_cache.shape:
+        raise KernelError("decode expects q [B,Hq,D] and caches [B,Hk,L,D]",
+                          context={"q": list(q.shape), "k": list(k_cache.shape), "v": list(v_cache.shape)})
+    B, Hq, D = q.shape
+    Hk, Lc = k_cache.shape[1], k_cache.shape[2]
+    if Hq % Hk or k_cache.shape[0] != B or k_cache.shape[3] != D:
+        raise KernelError("decode shape mismatch", context={"q": list(q.shape), "k": list(k_cache.shape)})
+    q = q.contiguous()
+    k_cache = k_cache.contiguous()
+    v_cache = v_cache.contiguous()
+    idx = kept.idx.contiguous()
+    cnt = kept.cnt.contiguous()
+    if out is None and partials is None:
+        out = torch.empty_like(q)
+    ws_ptr, ws_bytes = None, 0
+    if num_splits != 1:
+        if workspace is None:
+            ms = num_splits if num_splits > 0 else 64
+            workspace = DecodeWorkspace(B, Hq, Hk, D, ms, q.device)
+        ws_ptr, ws_bytes = workspace.buf.data_ptr(), workspace.bytes
+        if num_splits <= 0:
+            num_splits = min(workspace.max_splits, default_splits(B, Hk, idx.shape[-1] / 4))
+    args = L.DecodeArgs(
+        q=q.data_ptr(), k_cache=k_cache.data_ptr(), v_cache=v_cache.data_ptr(), out=L.ptr(out),
+        q_stride=L.strides3(q), k_stride=L.strides4(k_cache), v_stride=L.strides4(v_cache),
+        o_stride=L.strides3(out) if out is not None else L.I64x3(0, 0, 0),
+        B=B, Hq=Hq, Hk=Hk, L=Lc, D=D, block=block, dtype=L.dtype_code(q), scale=1.0 / math.sqrt(D),
+        kv_len=kv_len.data_ptr(), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(), nb_max=idx.shape[-1],
+        num_splits=num_splits, part_o=L.ptr(partials[0]) if partials else None,
+        part_ml=L.ptr(partials[1]) if partials else None, workspace=ws_ptr, workspace_bytes=ws_bytes,
+        err=L.ptr(err),
+    )
+    L.check(L.lib().tasft_bsa_decode_fwd(args, L.stream_ptr(q.device)), "tasft_bsa_decode_fwd",
+            shape=[B, Hq, Hk, Lc, D], splits=num_splits)
+    return out
+
+
+def decode_combine(part_o: torch.Tensor, part_ml: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """Merge G partials ``o [G,B,Hq,D]`` / ``ml [G,B,Hq,2]`` (e.g. all-gathered from G GPUs)."""
+    L.require_cuda(part_o, part_ml)
+    G = part_o.shape[0]
+    D = part_o.shape[-1]
+    rows = part_o[0].numel() // D
+    out = torch.empty(part_o.shape[1:], dtype=out_dtype, device=part_o.device)
+    po = part_o.float().contiguous()
+    pm = part_ml.float().contiguous()
+    args = L.CombineArgs(part_o=po.data_ptr(), part_ml=pm.data_ptr(), G=G, rows=rows, D=D, out=out.data_ptr(),
+                         dtype=L.dtype_code(out))
+    L.check(L.lib().tasft_bsa_decode_combine(args, L.stream_ptr(po.device)), "tasft_bsa_decode_combine")
+    return out
+
+
+__all__ = ["DecodeWorkspace", "bsa_decode", "decode_combine", "default_splits"]
