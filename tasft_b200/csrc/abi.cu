@@ -2,8 +2,25 @@
 // version and launch accounting.
 #include "common.cuh"
 
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+
 namespace tasft {
 std::atomic<int64_t> g_launches{0};
+
+bool debug_enabled() {
+  static const bool on = std::getenv("TASFT_DEBUG") != nullptr;
+  return on;
+}
+void debug_log(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  std::fprintf(stderr, "[tasft_b200] ");
+  std::vfprintf(stderr, fmt, ap);
+  std::fprintf(stderr, "\n");
+  va_end(ap);
+}
 int prefill_simt(const tasft_prefill_args& a, cudaStream_t st);
 // Returns TASFT_ERR_UNSUPPORTED when the tcgen05 kernel does not cover the shape.
 int prefill_tc(const tasft_prefill_args& a, cudaStream_t st);

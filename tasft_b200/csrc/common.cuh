@@ -15,7 +15,13 @@ namespace tasft {
 extern std::atomic<int64_t> g_launches;
 inline void count_launch(int n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
-inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? TASFT_OK : TASFT_ERR_CUDA; }
+bool debug_enabled();  // TASFT_DEBUG set in the environment
+void debug_log(const char* fmt, ...);
+
+inline int cuda_status(cudaError_t e) {
+  if (e != cudaSuccess && debug_enabled()) debug_log("CUDA error: %s", cudaGetErrorString(e));
+  return e == cudaSuccess ? TASFT_OK : TASFT_ERR_CUDA;
+}
 inline int launch_status() { return cuda_status(cudaGetLastError()); }
 
 // ---- element conversions --------------------------------------------------

@@ -11,7 +11,7 @@
 // accumulate p.V. All consumer warps share the running max, so their partial sums add
 // without rescaling. Splits of one unit are merged by the last CTA to finish
 // (an atomic ticket; no CTA ever waits on another).
-#include "common.cuh"
+#include "decode.cuh"
 
 namespace tasft {
 
@@ -19,16 +19,8 @@ constexpr int kDecConsumerWarps = 4;
 constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
 constexpr int kGmax = 8;  // max q-heads per kv-head handled by one CTA
 
-struct DecodeWs {
-  float* part;      // [B*Hq, max_splits, D + 2]  (normalised o, m, l)
-  int32_t* ticket;  // [B*Hk]
-  int max_splits;
-};
-
-__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-
 template <typename T, int D>
-__global__ void __launch_bounds__(kDecThreads) bsa_decode_kernel(tasft_decode_args a, DecodeWs ws, int nsplit,
+__global__ void __launch_bounds__(kDecThreads) bsa_decode_simt_kernel(tasft_decode_args a, DecodeWs ws, int nsplit,
                                                                  int nst) {
   constexpr int EPL = 16 / sizeof(T);   // elements per 16-byte lane load
   constexpr int LPK = D / EPL;          // lanes per key row
@@ -244,82 +236,23 @@ __global__ void __launch_bounds__(kDecThreads) bsa_decode_kernel(tasft_decode_ar
     }
     named_bar(1, kDecConsumerWarps * 32);
     const float* tot = red + kDecConsumerWarps * kGmax * (D + 1);
-    float mrow[kGmax];
+    // per-head (o / l, m, l) for the shared finish (m is already in base-e units here)
+    float* res = red + (kDecConsumerWarps + 1) * kGmax * (D + 1);
+    for (int x = tid; x < grp * (D + 2); x += kDecConsumerWarps * 32) {
+      const int g = x / (D + 2), d = x % (D + 2);
+      const float l = tot[g * (D + 1) + D];
+      float v;
+      if (d < D) v = l > 0.f ? tot[g * (D + 1) + d] / l : 0.f;
+      else if (d == D) {
+        float mm = -INFINITY;
 #pragma unroll
-    for (int g = 0; g < kGmax; ++g) mrow[g] = m_run[g];
-    if (nsplit == 1) {
-      for (int x = tid; x < grp * D; x += kDecConsumerWarps * 32) {
-        const int g = x / D, d = x % D;
-        const float l = tot[g * (D + 1) + D];
-        const float o = l > 0.f ? tot[g * (D + 1) + d] / l : 0.f;
-        const int hq = hk * grp + g;
-        if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(o);
-        const int64_t row = (int64_t)b * a.Hq + hq;
-        if (a.part_o) a.part_o[row * D + d] = o;
-        if (a.part_ml && d == 0) {
-          float mm = -INFINITY;
-#pragma unroll
-          for (int gg = 0; gg < kGmax; ++gg) if (gg == g) mm = mrow[gg];
-          a.part_ml[row * 2] = mm;
-          a.part_ml[row * 2 + 1] = l;
-        }
-      }
-    } else {
-      // write this split's partial, then take a ticket; the last split merges
-      for (int x = tid; x < grp * (D + 2); x += kDecConsumerWarps * 32) {
-        const int g = x / (D + 2), d = x % (D + 2);
-        const float l = tot[g * (D + 1) + D];
-        float v;
-        if (d < D) v = l > 0.f ? tot[g * (D + 1) + d] / l : 0.f;
-        else if (d == D) {
-          float mm = -INFINITY;
-#pragma unroll
-          for (int gg = 0; gg < kGmax; ++gg) if (gg == g) mm = mrow[gg];
-          v = mm;
-        } else v = l;
-        const int64_t row = (int64_t)b * a.Hq + hk * grp + g;
-        ws.part[(row * ws.max_splits + split) * (D + 2) + d] = v;
-      }
-      __threadfence();
-      named_bar(1, kDecConsumerWarps * 32);
-      if (tid == 0) {
-        const int prev = atomicAdd(&ws.ticket[unit], 1);
-        const int last = prev == nsplit - 1;
-        if (last) ws.ticket[unit] = 0;  // ready for the next call
-        s_last = last;
-      }
-      named_bar(1, kDecConsumerWarps * 32);
-      if (s_last) {
-        __threadfence();
-        for (int x = tid; x < grp * D; x += kDecConsumerWarps * 32) {
-          const int g = x / D, d = x % D;
-          const int64_t row = (int64_t)b * a.Hq + hk * grp + g;
-          const float* pr = ws.part + row * ws.max_splits * (D + 2);
-          float mt = -INFINITY;
-          for (int sp = 0; sp < nsplit; ++sp) {
-            const float l = __ldcg(pr + sp * (D + 2) + D + 1);
-            if (l > 0.f) mt = fmaxf(mt, __ldcg(pr + sp * (D + 2) + D));
-          }
-          float num = 0.f, den = 0.f;
-          for (int sp = 0; sp < nsplit; ++sp) {
-            const float l = __ldcg(pr + sp * (D + 2) + D + 1);
-            if (l > 0.f) {
-              const float w = l * __expf(__ldcg(pr + sp * (D + 2) + D) - mt);
-              num = fmaf(w, __ldcg(pr + sp * (D + 2) + d), num);
-              den += w;
-            }
-          }
-          const float o = den > 0.f ? num / den : 0.f;
-          const int hq = hk * grp + g;
-          if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(o);
-          if (a.part_o) a.part_o[row * D + d] = o;
-          if (a.part_ml && d == 0) {
-            a.part_ml[row * 2] = mt;
-            a.part_ml[row * 2 + 1] = den;
-          }
-        }
-      }
+        for (int gg = 0; gg < kGmax; ++gg) if (gg == g) mm = m_run[gg];
+        v = mm;
+      } else v = l;
+      res[x] = v;
     }
+    named_bar(1, kDecConsumerWarps * 32);
+    decode_finish<T>(a, ws, nsplit, split, unit, b, hk, grp, res, tid, kDecConsumerWarps * 32, 1, &s_last);
   }
 }
 
@@ -355,7 +288,7 @@ static int decode_stages(int block, int D, int esize) {
 static size_t decode_smem(int block, int D, int esize, int nst) {
   size_t s = (size_t)nst * 2 * block * D * esize + (size_t)kGmax * block * 4;
   s = (s + 15) / 16 * 16 + (size_t)2 * nst * 8;
-  const size_t red = (size_t)(kDecConsumerWarps + 1) * kGmax * (D + 1) * 4;
+  const size_t red = ((size_t)(kDecConsumerWarps + 1) * kGmax * (D + 1) + (size_t)kGmax * (D + 2)) * 4;
   const size_t ring = (size_t)nst * 2 * block * D * esize;
   if (red > ring) s += red - ring;  // reduction buffer aliases the ring
   return s;
@@ -365,7 +298,7 @@ template <typename T, int D>
 static int launch_decode_t(const tasft_decode_args& a, DecodeWs ws, int nsplit, cudaStream_t st) {
   const int nst = decode_stages(a.block, D, sizeof(T));
   const size_t smem = decode_smem(a.block, D, sizeof(T), nst);
-  auto kern = bsa_decode_kernel<T, D>;
+  auto kern = bsa_decode_simt_kernel<T, D>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return TASFT_ERR_CUDA;
   const int64_t grid = (int64_t)a.B * a.Hk * nsplit;
@@ -439,6 +372,10 @@ extern "C" int tasft_bsa_decode_fwd(const tasft_decode_args* ap, tasft_stream_t 
     if (rc != TASFT_OK) return rc;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (a.dtype != TASFT_F32) {
+    const int rc = decode_mma(a, ws, nsplit, st);
+    if (rc != TASFT_ERR_UNSUPPORTED) return rc;
+  }
   switch (a.dtype) {
     case TASFT_F32: return launch_decode_dt<float>(a, ws, nsplit, st);
     case TASFT_BF16: return launch_decode_dt<__nv_bfloat16>(a, ws, nsplit, st);

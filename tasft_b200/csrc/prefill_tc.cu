@@ -50,7 +50,7 @@ struct Smem {
   static constexpr int kListOff = kStageOff + 2 * kStageBytes;
   static constexpr int kBitmapOff = kListOff + kMaxNB * 4;
   static constexpr int kBarOff = kBitmapOff + 2 * (kMaxNB / 32) * 4;
-  static constexpr int kNumBars = 10;
+  static constexpr int kNumBars = 11;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
@@ -106,6 +106,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* p_ready = bars + 7;   // [2]
   uint64_t* pv_done = bars + 9;
+  // Single-use barrier for the epilogue. pv_done cannot serve: when the softmax warps
+  // finish the last block, P.V of block n-2 may still run, and a parity wait cannot tell
+  // "phase n-2 pending" from "phase n-1 done".
+  uint64_t* o_final = bars + 10;
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);  // [0] tmem base, [1] list length, [2] abort
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -122,6 +126,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&p_ready[i], 128);
     }
     mbar_init(pv_done, 1);
+    mbar_init(o_final, 1);
     fence_barrier_init();
     misc[2] = 0;
   }
@@ -255,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc::mma_commit(&kv_empty[j & 1]);
         tc::mma_commit(pv_done);
+        if (j == n - 1) tc::mma_commit(o_final);
       }
       if (!ok) {
         set_err(a.err, TASFT_DEVERR_TIMEOUT);
@@ -278,13 +284,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int kb = entry & 0xffff;
       const bool active = w.valid[slot] && ((entry >> (16 + slot)) & 1);
       uint32_t sraw[64];
-      {
-        uint32_t (&h0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]);
-        uint32_t (&h1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]);
-        tc::tmem_ld32(tS0 + (j & 1) * 64 + lane_off, h0);
-        tc::tmem_ld32(tS0 + (j & 1) * 64 + 32 + lane_off, h1);
-        tc::tmem_wait_ld();
-      }
+      tc::tmem_ld64_sync(tS0 + (j & 1) * 64 + lane_off, sraw);
       const int kbase = kb * kBlk;
       // keys valid for this row: < S, and <= qpos when causal
       int lim = a.S - kbase;
@@ -309,8 +309,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float alpha = need ? ex2(m - m_new) : 1.0f;
         for (int c0 = 0; c0 < D; c0 += 32) {
           uint32_t o[32];
-          tc::tmem_ld32(tO + c0 + lane_off, o);
-          tc::tmem_wait_ld();
+          tc::tmem_ld32_sync(tO + c0 + lane_off, o);
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
           tc::tmem_st32(tO + c0 + lane_off, o);
@@ -337,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(&p_ready[j & 1]);
     }
     if (ok && n > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (n - 1) & 1));
+      ok = __all_sync(0xffffffffu, mbar_wait(o_final, 0));
       tc::tc_fence_after();
     }
     if (!ok) set_err(a.err, TASFT_DEVERR_TIMEOUT);
@@ -350,8 +349,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int c0 = 0; c0 < D; c0 += 32) {
       uint32_t o[32];
       if (n > 0) {
-        tc::tmem_ld32(tO + c0 + lane_off, o);
-        tc::tmem_wait_ld();
+        tc::tmem_ld32_sync(tO + c0 + lane_off, o);
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) o[c] = 0u;

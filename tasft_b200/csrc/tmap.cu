@@ -38,6 +38,7 @@ bool make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int S, int
   const CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS && debug_enabled()) debug_log("cuTensorMapEncodeTiled failed: %d", (int)r);
   return r == CUDA_SUCCESS;
 }
 

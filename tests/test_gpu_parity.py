@@ -135,6 +135,8 @@ class TestPrefill:
         (1, 4, 4, 448, 64, 0.3, False),    # MHA D64: slots are q-block pairs
         (1, 4, 2, 512, 128, 0.3, True),    # per-q-head masks under GQA
         (2, 2, 2, 130, 64, 1.0, False),    # dense, tiny, ragged
+        (1, 4, 1, 2048, 128, 0.6, False),  # long kept lists: deep ring reuse
+        (1, 2, 2, 1536, 64, 1.0, False),   # dense MHA, 24 blocks per row
     ])
     def test_tc_bf16_vs_oracle(self, B, Hq, Hk, S, D, density, per_q):
         q, k, v, mask = _prefill_case(B, Hq, Hk, S, D, torch.bfloat16, density, seed=S + Hq, per_q_head=per_q)
@@ -144,6 +146,24 @@ class TestPrefill:
         ref = O.bsa_prefill_masked_dense(q, k, v, mask, 64, causal=True)
         assert int(err.item()) == 0
         assert_bf16_close(out, ref)
+
+    @pytest.mark.parametrize("gain", [6.0, 20.0])
+    def test_lazy_rescale_path(self, gain):
+        """Large logits make the running max jump by > 2^8 (log2 units): O gets rescaled."""
+        q, k, v, mask = _prefill_case(1, 4, 1, 1024, 128, torch.bfloat16, 0.5, seed=31)
+        q = (q.float() * gain).to(torch.bfloat16)
+        # make late blocks dominate so the max keeps growing along each row
+        ramp = torch.linspace(0.2, 3.0, 1024).view(1, 1, 1024, 1)
+        k = (k.float() * ramp).to(torch.bfloat16)
+        out = T.BlockSparseFlashAttention().forward(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV))
+        assert_bf16_close(out, O.bsa_prefill_masked_dense(q, k, v, mask, 64))
+
+    def test_run_to_run_deterministic(self):
+        q, k, v, mask = _prefill_case(2, 8, 2, 2048, 128, torch.bfloat16, 0.3, seed=33)
+        kern = T.BlockSparseFlashAttention()
+        a = kern.forward(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV))
+        b = kern.forward(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV))
+        assert torch.equal(a, b)
 
     def test_tc_matches_simt(self):
         q, k, v, mask = _prefill_case(2, 8, 2, 1024, 128, torch.bfloat16, 0.2, seed=7)
