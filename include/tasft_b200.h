@@ -177,6 +177,17 @@ typedef struct {
 TASFT_API int64_t tasft_decode_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t D, int32_t max_splits);
 TASFT_API int tasft_bsa_decode_fwd(const tasft_decode_args* args, tasft_stream_t stream);
 
+/* Same computation as tasft_bsa_decode_fwd, for callers that cannot allocate device
+ * memory (a plugin whose host owns every allocation, a serving loop that must not call
+ * cudaMalloc). No counterpart in the reference. The split-KV scratch is a fixed
+ * per-device array of tasft_decode_noalloc_capacity() bytes (4 MiB) inside the library;
+ * args->workspace is ignored. The first call on a device looks the array up and should
+ * come before any stream capture. All calls on a device share the array: calls that
+ * overlap on the GPU race; order them on one stream. A call that needs more scratch than
+ * the capacity returns TASFT_ERR_TOO_LARGE without launching. Nothing is allocated. */
+TASFT_API int tasft_bsa_decode_fwd_noalloc(const tasft_decode_args* args, tasft_stream_t stream);
+TASFT_API int64_t tasft_decode_noalloc_capacity(void);
+
 /* Merge G partial results (normalised o, m, l) into the final output. */
 typedef struct {
   const float* part_o;    /* [G, rows, D] fp32 */

@@ -125,6 +125,8 @@ SIGNATURES = {
     "tasft_decode_workspace_size": ([C.c_int32] * 5, C.c_int64),
     "tasft_bsa_decode_fwd": ([C.POINTER(DecodeArgs), vp], C.c_int),
     "tasft_bsa_decode_combine": ([C.POINTER(CombineArgs), vp], C.c_int),
+    "tasft_bsa_decode_fwd_noalloc": ([C.POINTER(DecodeArgs), vp], C.c_int),
+    "tasft_decode_noalloc_capacity": ([], C.c_int64),
     "tasft_gate_target_workspace_size": ([C.c_int32] * 4, C.c_int64),
     "tasft_gate_target_fwd": ([C.POINTER(TargetArgs), vp], C.c_int),
     "tasft_gate_loss_workspace_size": ([C.c_int32] * 2, C.c_int64),

@@ -398,3 +398,53 @@ extern "C" int tasft_bsa_decode_combine(const tasft_combine_args* ap, tasft_stre
   count_launch();
   return launch_status();
 }
+
+// ---------------------------------------------------------------------------
+// Helpers for entry points that bring their own scratch (decode_noalloc.cu). They
+// repeat the argument checks, split choice and kernel dispatch of tasft_bsa_decode_fwd.
+// ---------------------------------------------------------------------------
+namespace tasft {
+
+int decode_check_args(const tasft_decode_args& a) {
+  if (!a.q || !a.k_cache || !a.v_cache || !a.kv_len || !a.kept_idx || !a.kept_cnt) return TASFT_ERR_INVALID_ARG;
+  if (!a.out && !a.part_o) return TASFT_ERR_INVALID_ARG;
+  if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.L <= 0 || a.block <= 0 || a.nb_max <= 0) return TASFT_ERR_INVALID_ARG;
+  if (a.Hq % a.Hk != 0 || a.Hq / a.Hk > kGmax) return TASFT_ERR_UNSUPPORTED;
+  if (a.block > 128 || a.block % 8 != 0) return TASFT_ERR_UNSUPPORTED;
+  const int es = elem_size(a.dtype);
+  if (a.k_stride[3] != 1 || a.v_stride[3] != 1 || a.k_stride[2] != a.D || a.v_stride[2] != a.D ||
+      a.q_stride[2] != 1 || (a.out && a.o_stride[2] != 1))
+    return TASFT_ERR_INVALID_ARG;
+  if (!aligned16(a.k_cache) || !aligned16(a.v_cache) || !aligned16(a.q) || (a.k_stride[1] * es) % 16 ||
+      (a.v_stride[1] * es) % 16 || (a.k_stride[0] * es) % 16 || (a.v_stride[0] * es) % 16 ||
+      (a.q_stride[1] * es) % 16 || (a.q_stride[0] * es) % 16)
+    return TASFT_ERR_INVALID_ARG;
+  return TASFT_OK;
+}
+
+int decode_pick_splits(const tasft_decode_args& a) {
+  int nsplit = a.num_splits;
+  if (nsplit <= 0) {
+    const int units = a.B * a.Hk;
+    nsplit = (4 * 148 + units - 1) / units;
+    const int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
+    if (nsplit > cap) nsplit = cap;
+    if (nsplit < 1) nsplit = 1;
+  }
+  return nsplit;
+}
+
+int decode_run(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st) {
+  if (a.dtype != TASFT_F32) {
+    const int rc = decode_mma(a, ws, nsplit, st);
+    if (rc != TASFT_ERR_UNSUPPORTED) return rc;
+  }
+  switch (a.dtype) {
+    case TASFT_F32: return launch_decode_dt<float>(a, ws, nsplit, st);
+    case TASFT_BF16: return launch_decode_dt<__nv_bfloat16>(a, ws, nsplit, st);
+    case TASFT_F16: return launch_decode_dt<__half>(a, ws, nsplit, st);
+    default: return TASFT_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace tasft
