@@ -56,7 +56,11 @@ def load_traffic():
 
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi sampling during the timed region (clocks + throttle reasons)."""
+    """nvidia-smi polled every 200 ms during the timed region (clocks + throttle reasons).
+
+    One-shot queries from a thread: a long-running `nvidia-smi -lms` writing into a pipe
+    is block-buffered and loses its samples when it is stopped.
+    """
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -64,31 +68,27 @@ class ClockSampler:
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
         self.lines: list[str] = []
+        self._stop = threading.Event()
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except OSError:
-            self.proc = None
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                r = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                    "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                self.lines.extend(ln.strip() for ln in r.stdout.splitlines() if ln.strip())
+            except (OSError, subprocess.SubprocessError):
+                return
+            self._stop.wait(0.2)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        self.t.join(timeout=10)
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -299,9 +299,9 @@ def run_ours(args):
     def step():
         kern.forward(q, k, v, mask, out=out)
 
+    clk = ClockSampler(local).__enter__()  # sampled across all timed phases
     n0 = L.launch_count()
-    with ClockSampler(local) as clk:
-        t_step = time_steps(step, args.steps, args.warmup, flush, ws)
+    t_step = time_steps(step, args.steps, args.warmup, flush, ws)
     launches = (L.launch_count() - n0) // (args.steps + args.warmup)
     ms = statistics.mean(t_step)
     ms_max = max_over_ranks(ms, ws)
@@ -353,6 +353,7 @@ def run_ours(args):
         T.bsa_decode(qd, kc, vc, kv_len, dkept, DEC["block"], num_splits=splits, workspace=wsp, out=od)
 
     t_dec = time_steps(dstep, args.steps, args.warmup, flush, ws)
+    clk.__exit__(None, None, None)
     ms_d = statistics.mean(t_dec)
     ms_d_max = max_over_ranks(ms_d, ws)
     kept_dec = int(dkept.cnt.sum().item())
