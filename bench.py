@@ -320,6 +320,21 @@ def run_ours(args):
                 "algorithmic": f"{flops / 1e9:.2f} GFLOP per launch (kept blocks x 4*64*64*128 x 4 q-heads)",
                 "ms_per_launch": round(ms_k, 4)}
 
+    # ---------------- gate mask build (HBM-bound: reads Q and K once) ----------------
+    def gstep():
+        with torch.no_grad():
+            _gate(q, k)
+
+    t_gate = time_steps(gstep, args.steps, args.warmup, flush, ws)
+    ms_g = statistics.mean(t_gate)
+    gbytes = (q.numel() + k.numel()) * 2
+    gate_info = {"ms_per_step": round(ms_g, 4), "kernels": "gate_pool_project_kernel + gate_pair_kernel",
+                 "roofline": {"bound": "hbm", "achieved": round(gbytes / (ms_g * 1e-3) / 1e9, 1),
+                              "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                              "frac": round(gbytes / (ms_g * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                              "traffic": traffic.get("gate_pool"),
+                              "algorithmic": f"{gbytes / 1e6:.1f} MB per step (|Q| + |K|)"}}
+
     # ---------------- e2e through the public API with host buffers ----------------
     qh = q.cpu().pin_memory()
     kh = k.cpu().pin_memory()
@@ -364,7 +379,7 @@ def run_ours(args):
               "kept_blocks_per_seq_head": round(mean_kept, 2),
               "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                            "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": traffic.get("decode"),
-                           "peak_src": peaks["src"], "kernel": "bsa_decode_kernel",
+                           "peak_src": peaks["src"], "kernel": "bsa_decode_mma_kernel",
                            "algorithmic": f"{dbytes / 1e6:.1f} MB per launch (kept K+V blocks + q + out)"}}
 
     cpu = None
@@ -388,6 +403,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 3),
                     "api": "tasft_b200.BlockSparseFlashAttention.forward(q, k, v, bool mask) from pinned host"},
             "decode": decode,
+            "gate": gate_info,
             "gpu_launches": launches * args.steps,
             "gpu_launches_per_step": launches,
             "clocks": clk.summary(),
@@ -400,6 +416,34 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_only(args):
+    """Launch one kernel family `--steps` times on the bench workload (for ncu captures)."""
+    import tasft_b200 as T  # noqa: PLC0415
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.only == "decode":
+        qd, kc, vc, kv_len, kept = make_decode_inputs(1237, dev)
+        splits = T.decode.default_splits(DEC["B"], DEC["Hk"], float(kept.cnt.float().mean().item()))
+        wsp = T.DecodeWorkspace(DEC["B"], DEC["Hq"], DEC["Hk"], DEC["D"], splits, dev)
+        for _ in range(args.steps):
+            T.bsa_decode(qd, kc, vc, kv_len, kept, DEC["block"], num_splits=splits, workspace=wsp)
+    else:
+        q, k, v, mask, gate = make_prefill_inputs(1236, dev)
+        kern = T.BlockSparseFlashAttention(block_size=CFG["block"])
+        kept = T.mask_to_kept(mask, True)
+        for _ in range(args.steps):
+            if args.only == "prefill":
+                kern.forward(q, k, v, kept)
+            elif args.only == "gate":
+                with torch.no_grad():
+                    gate(q, k)
+            else:
+                T.gate_target_from_qk(q[:1], k[:1], CFG["block"])
+    torch.cuda.synchronize()
+    print(f"{args.only}: {args.steps} launches ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -408,9 +452,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--only", choices=["prefill", "decode", "gate", "target"],
+                    help="profiling driver: run `--steps` launches of one kernel family, print nothing else")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

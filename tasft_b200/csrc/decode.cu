@@ -322,16 +322,16 @@ using namespace tasft;
 
 extern "C" int64_t tasft_decode_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t D, int32_t max_splits) {
   if (B <= 0 || Hq <= 0 || Hk <= 0 || D <= 0 || max_splits <= 0) return -1;
-  const int64_t tick = ((int64_t)B * Hk * 4 + 255) / 256 * 256;
+  const int64_t tick = ((int64_t)(B * Hk + 2) * 4 + 255) / 256 * 256;
   const int64_t part = (int64_t)B * Hq * max_splits * (D + 2) * 4;
   return tick + (part + 255) / 256 * 256;
 }
 
-// Workspace layout: [tickets: B*Hk int32, padded to 256 B][partials: B*Hq x nsplit x (D+2) fp32].
+// Workspace layout: [tickets: B*Hk int32 + 2 work counters, padded to 256 B][partials: B*Hq x nsplit x (D+2) fp32].
 // Tickets sit first so their place does not depend on the split count; every call
 // leaves them at zero again.
 static int decode_ws_from(const tasft_decode_args& a, int nsplit, DecodeWs* ws) {
-  const int64_t tick = ((int64_t)a.B * a.Hk * 4 + 255) / 256 * 256;
+  const int64_t tick = ((int64_t)(a.B * a.Hk + 2) * 4 + 255) / 256 * 256;
   const int64_t need = tick + (int64_t)a.B * a.Hq * nsplit * (a.D + 2) * 4;
   if (a.workspace_bytes < need) return TASFT_ERR_WORKSPACE;
   ws->max_splits = nsplit;
@@ -360,7 +360,7 @@ extern "C" int tasft_bsa_decode_fwd(const tasft_decode_args* ap, tasft_stream_t 
   int nsplit = a.num_splits;
   if (nsplit <= 0) {
     const int units = a.B * a.Hk;
-    nsplit = (4 * 148 + units - 1) / units;
+    nsplit = (6 * 148) / units;  // items within the resident CTA slots
     const int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
     if (nsplit > cap) nsplit = cap;
     if (nsplit < 1) nsplit = 1;
@@ -426,7 +426,7 @@ int decode_pick_splits(const tasft_decode_args& a) {
   int nsplit = a.num_splits;
   if (nsplit <= 0) {
     const int units = a.B * a.Hk;
-    nsplit = (4 * 148 + units - 1) / units;
+    nsplit = (6 * 148) / units;  // items within the resident CTA slots
     const int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
     if (nsplit > cap) nsplit = cap;
     if (nsplit < 1) nsplit = 1;

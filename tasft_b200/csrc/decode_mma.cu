@@ -5,26 +5,32 @@
 // small (CUDA-core dot products with shuffle reductions issued ~14K warp instructions
 // per 32 KB block; this path issues a few hundred).
 //
-//   CTA = (sequence, kv-head, split); 2 warps: warp 1 = TMA producer, warp 0 = the one
-//   consumer, 3 CTAs per SM. K/V tiles arrive through a 2-stage ring of 128B-swizzled
-//   TMA boxes (64 rows x 64 elements), so ldmatrix reads are conflict free. A single
-//   in-order consumer per ring keeps every mbarrier parity wait exact: with several
-//   consumers taking turns on a shared ring, a fast one can reach a stage two phases
-//   ahead of its barrier, where a parity wait cannot tell the phases apart.
-//   Per block and warp:  S[16 x 64] = Qpad[16 x D] K^T (q-heads in rows, zero padded),
-//   fp32 online softmax in base 2, P rounded to the value dtype as the reference kernel
-//   does (tasft/kernels/block_sparse_fa.py:252), O[16 x D] += P V.
-//   Splits of one (sequence, kv-head) merge via decode_finish.
+//   Persistent CTAs (every resident slot, 6 per SM), 2 warps each: warp 1 = TMA
+//   producer, warp 0 = the one consumer. Work items are (sequence, kv-head, split)
+//   slices of the kept lists; the producer claims them from a counter in the workspace
+//   (dynamic balance; a static stride when there is no workspace), tags every ring entry
+//   with (item, half-block) and streams all items through one ring, so the pipeline never
+//   drains between items. K/V half-blocks (32 keys) arrive in a 2-stage ring of
+//   128B-swizzled TMA boxes, so ldmatrix reads are conflict free. A single in-order
+//   consumer per ring keeps every mbarrier parity wait exact: with several consumers
+//   taking turns on a shared ring, a fast one can reach a stage two phases ahead of its
+//   barrier, where a parity wait cannot tell the phases apart.
+//   Per stage: S^T[32 keys x 8 heads] = K Q^T (keys in the MMA's M, the group's q-heads
+//   in N), fp32 online softmax in base 2, P rounded to the value dtype as the reference
+//   kernel does (tasft/kernels/block_sparse_fa.py:252) and turned into the B operand with
+//   movmatrix.trans, O^T[D x 8] += V^T P^T. Splits of one (sequence, kv-head) merge
+//   through an atomic ticket: the last split to finish merges all partials.
 #include "decode.cuh"
 #include "tc.cuh"
 
 namespace tasft {
 namespace {
 
-constexpr int kConsumers = 1;
-constexpr int kThreadsM = (kConsumers + 1) * 32;
+constexpr int kThreadsM = 64;    // warp 0 consumer, warp 1 producer
 constexpr int kStages = 2;
-constexpr int kBlkM = 64;
+constexpr int kBlkM = 64;        // kv block (list granularity)
+constexpr int kSub = 32;         // keys per ring stage (half a block)
+constexpr int kCtasPerSm = 6;
 constexpr float kLog2eM = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -65,40 +71,68 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 }
 
 // byte offset of 16-byte chunk `c` (0 .. D/8-1) of tile row `r` in a 128B-swizzled tile
-// made of D/64 regions of [64 rows x 128 B]
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-  return (uint32_t)((c >> 3) * (kBlkM * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+// made of D/64 regions of [32 rows x 128 B]
+__device__ __forceinline__ uint32_t swz32(int r, int c) {
+  return (uint32_t)((c >> 3) * (kSub * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// Ring-entry tag written by the producer before it arms the stage's barrier; the
+// mbarrier arrive (release) / wait (acquire) pair makes it visible to the consumer.
+struct Tag {
+  int item;  // work item (unit * nsplit + split); -1 = no more work
+  int j;     // stage index within the item (two 32-key halves per kept block)
+  int n;     // stages in the item (0: empty item, finish only)
+  int kb;    // kv block index; the half is j & 1
+};
+
+// Claim the next work item: a global counter when the workspace provides one (dynamic
+// balance), else a static stride over the grid.
+__device__ __forceinline__ int next_item(int32_t* ctr, int& k, int items) {
+  int it;
+  if (ctr) {
+    it = atomicAdd(ctr, 1);
+    if (it >= items) {
+      // the last CTA to run out resets both counters for the next launch
+      if (atomicAdd(ctr + 1, 1) == (int)gridDim.x - 1) {
+        atomicExch(ctr, 0);
+        atomicExch(ctr + 1, 0);
+      }
+      return -1;
+    }
+    return it;
+  }
+  it = blockIdx.x + (k++) * gridDim.x;
+  return it < items ? it : -1;
+}
+
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
 template <int D, bool kF16>
-__global__ void __launch_bounds__(kThreadsM, 3)
+__global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
     bsa_decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                           const tasft_decode_args a, const DecodeWs ws, const int nsplit) {
   using T = typename std::conditional<kF16, __half, __nv_bfloat16>::type;
-  constexpr int kTile = (D / 64) * kBlkM * 128;  // bytes of one K (or V) tile
+  constexpr int kTile = (D / 64) * kSub * 128;  // bytes of one K (or V) half-block tile
   constexpr int kStage = 2 * kTile;
-  constexpr int NT = kBlkM / 8;   // key n-tiles per block
-  constexpr int KS = D / 16;      // k-steps over D
-  constexpr int DT = D / 8;       // dim n-tiles of O
+  constexpr int KS = D / 16;   // k-steps over D (S^T = K Q^T)
+  constexpr int MD = D / 16;   // m-tiles over D (O^T = V^T P^T)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
   uint64_t* empty = full + kStages;
-  __shared__ int s_last;
+  Tag* tags = reinterpret_cast<Tag*>(empty + kStages);
 
-  const int unit = blockIdx.x / nsplit;
-  const int split = blockIdx.x % nsplit;
-  const int b = unit / a.Hk, hk = unit % a.Hk;
   const int grp = a.Hq / a.Hk;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cnt_all = a.kept_cnt[(int64_t)b * a.Hk + hk];
-  const int t0 = (int)((int64_t)split * cnt_all / nsplit);
-  const int t1 = (int)((int64_t)(split + 1) * cnt_all / nsplit);
-  const int n = t1 - t0;
-  const int32_t* list = a.kept_idx + ((int64_t)b * a.Hk + hk) * a.nb_max + t0;
-  const int kvlen = min(a.kv_len[b], a.L);
+  const int items = a.B * a.Hk * nsplit;
   const int NBk = (a.L + kBlkM - 1) / kBlkM;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // dynamic claiming only pays when there are more items than resident CTAs
+  int32_t* ctr = (ws.ticket && items > (int)gridDim.x) ? ws.ticket + (int64_t)a.B * a.Hk : nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -109,209 +143,261 @@ __global__ void __launch_bounds__(kThreadsM, 3)
   }
   __syncthreads();
 
-  if (warp == kConsumers) {
-    // ---------------- producer ----------------
+  if (warp == 1) {
+    // ---------------- producer: streams every claimed item's half-blocks ----------------
     if (lane == 0) {
       tc::prefetch_tmap(&tmk);
       tc::prefetch_tmap(&tmv);
-      int issued = 0;
-      for (int i = 0; i < n; ++i) {
-        const int s = i % kStages;
-        if (i >= kStages && !mbar_wait(&empty[s], ((i / kStages) - 1) & 1)) {
+      int r = 0, k = 0;
+      bool alive = true;
+      auto push = [&](const Tag& t) -> bool {
+        const int s = r % kStages;
+        if (r >= kStages && !mbar_wait(&empty[s], ((r / kStages) - 1) & 1)) {
           set_err(a.err, TASFT_DEVERR_TIMEOUT);
-          break;
+          return false;
         }
-        const int kb = list[i];
-        if (kb >= 0 && kb < NBk) {
+        tags[s] = t;
+        if (t.item >= 0 && t.n > 0 && t.kb >= 0 && t.kb < NBk) {
+          const int unit = t.item / nsplit;
+          const int b = unit / a.Hk, hk = unit % a.Hk;
+          const int row = t.kb * kBlkM + (t.j & 1) * kSub;
           uint8_t* sk = smem + s * kStage;
           mbar_arrive_expect_tx(&full[s], kStage);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c) {
-            tc::tma_load_4d(sk + c * kBlkM * 128, &tmk, c * 64, kb * kBlkM, hk, b, &full[s]);
-            tc::tma_load_4d(sk + kTile + c * kBlkM * 128, &tmv, c * 64, kb * kBlkM, hk, b, &full[s]);
+            tc::tma_load_4d(sk + c * kSub * 128, &tmk, c * 64, row, hk, b, &full[s]);
+            tc::tma_load_4d(sk + kTile + c * kSub * 128, &tmv, c * 64, row, hk, b, &full[s]);
           }
         } else {
           mbar_arrive(&full[s]);
         }
-        ++issued;
+        ++r;
+        return true;
+      };
+      // claim one item ahead so the counter's round trip overlaps the current pushes
+      int nxt = next_item(ctr, k, items);
+      while (alive) {
+        const int it = nxt;
+        if (it < 0) {
+          push(Tag{-1, 0, 0, -1});
+          break;
+        }
+        nxt = next_item(ctr, k, items);
+        const int unit = it / nsplit, split = it % nsplit;
+        const int cnt_all = a.kept_cnt[unit];
+        const int t0 = (int)((int64_t)split * cnt_all / nsplit);
+        const int n = (int)((int64_t)(split + 1) * cnt_all / nsplit) - t0;
+        const int32_t* list = a.kept_idx + (int64_t)unit * a.nb_max + t0;
+        if (n == 0) {
+          alive = push(Tag{it, 0, 0, -1});
+        } else {
+          for (int j = 0; j < 2 * n && alive; ++j) alive = push(Tag{it, j, 2 * n, list[j >> 1]});
+        }
       }
-      for (int i = max(0, issued - kStages); i < issued; ++i) mbar_wait(&full[i % kStages], (i / kStages) & 1);
+      for (int i = max(0, r - kStages); i < r; ++i) mbar_wait(&full[i % kStages], (i / kStages) & 1);
     }
   } else {
-    // ---------------- consumers ----------------
+    // ---------------- consumer: follows the tags ----------------
+    // Thread (g, tig) = (lane / 4, lane % 4) owns q-heads 2 tig and 2 tig + 1 (columns of
+    // S^T and O^T), keys g and g + 8 of each 16-key m-tile, dims g and g + 8 of each
+    // 16-dim m-tile of O^T.
     const int g = lane >> 2, tig = lane & 3;
-    // Q as the A operand: rows = q-heads of the group (g and g + 8), zero padded
-    uint32_t qa[KS][4];
-    {
-      const T* Q = reinterpret_cast<const T*>(a.q) + b * a.q_stride[0];
-      const bool r0 = g < grp, r1 = g + 8 < grp;
-      const T* q0 = Q + (int64_t)(hk * grp + g) * a.q_stride[1];
-      const T* q1 = Q + (int64_t)(hk * grp + g + 8) * a.q_stride[1];
-#pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        const int d0 = ks * 16 + 2 * tig;
-        qa[ks][0] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + d0) : 0u;
-        qa[ks][1] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + d0) : 0u;
-        qa[ks][2] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + d0 + 8) : 0u;
-        qa[ks][3] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + d0 + 8) : 0u;
-      }
-    }
     const float sl2 = a.scale * kLog2eM;
-    float o[DT][4];
-#pragma unroll
-    for (int t = 0; t < DT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g, g + 8 (base 2)
-    bool ok = true;
-    for (int i = warp; i < n; i += kConsumers) {
-      const int s = i % kStages;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (i / kStages) & 1))) {
-        ok = false;
+    uint32_t qb[KS][2];   // Q^T as the B operand: [D x 8 heads]
+    float o[MD][4];       // O^T accumulators
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    int cur = -1, kvlen = 0;
+    for (int r = 0;; ++r) {
+      const int s = r % kStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (r / kStages) & 1))) {
         set_err(a.err, TASFT_DEVERR_TIMEOUT);
         break;
       }
-      const int kb = list[i];
-      const bool kb_ok = kb >= 0 && kb < NBk;
-      if (!kb_ok) {
-        if (lane == 0) {
-          set_err(a.err, TASFT_DEVERR_INDEX);
-          mbar_arrive(&empty[s]);
+      const Tag t = tags[s];
+      if (t.item < 0) break;
+      const int unit = t.item / nsplit, split = t.item % nsplit;
+      const int b = unit / a.Hk, hk = unit % a.Hk;
+      if (t.item != cur) {
+        cur = t.item;
+        kvlen = min(a.kv_len[b], a.L);
+        const T* qh = reinterpret_cast<const T*>(a.q) + b * a.q_stride[0] + (int64_t)(hk * grp + g) * a.q_stride[1];
+        const bool hv = g < grp;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          qb[ks][0] = hv ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 2 * tig) : 0u;
+          qb[ks][1] = hv ? *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 8 + 2 * tig) : 0u;
         }
-        continue;
+#pragma unroll
+        for (int x = 0; x < MD; ++x) o[x][0] = o[x][1] = o[x][2] = o[x][3] = 0.f;
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.f;
       }
-      const uint32_t kbase = smem_u32(smem + s * kStage);
-      const uint32_t vbase = kbase + kTile;
-      // ---- S = Q K^T ----
-      float sc[NT][4];
+      const bool kb_ok = t.n > 0 && t.kb >= 0 && t.kb < NBk;
+      if (t.n > 0 && !kb_ok && lane == 0 && (t.j & 1) == 0) set_err(a.err, TASFT_DEVERR_INDEX);
+      if (kb_ok) {
+        const uint32_t kbase = smem_u32(smem + s * kStage);
+        const uint32_t vbase = kbase + kTile;
+        // ---- S^T [32 keys x 8 heads] = K Q^T ----
+        float sc[2][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-        const int row = nt * 8 + (lane & 7);
+        for (int mt = 0; mt < 2; ++mt) {
+          sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+          const int row = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-        for (int kp = 0; kp < KS / 2; ++kp) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(kbase + swz(row, kp * 4 + (lane >> 3)), b0, b1, b2, b3);
-          mma16816<kF16>(sc[nt], qa[2 * kp], b0, b1);
-          mma16816<kF16>(sc[nt], qa[2 * kp + 1], b2, b3);
+          for (int ks = 0; ks < KS; ++ks) {
+            uint32_t af[4];
+            ldsm_x4(kbase + swz32(row, 2 * ks + (lane >> 4)), af[0], af[1], af[2], af[3]);
+            mma16816<kF16>(sc[mt], af, qb[ks][0], qb[ks][1]);
+          }
         }
-      }
-      // ---- mask, scale, block max ----
-      const int kp0 = kb * kBlkM;
-      float mb0 = -INFINITY, mb1 = -INFINITY;
+        // ---- mask, scale, per-head max over the 32 keys ----
+        const int key0 = t.kb * kBlkM + (t.j & 1) * kSub;
+        float mb[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
+        for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // h: key g (c0, c1) or key g + 8 (c2, c3)
+            const bool valid = key0 + mt * 16 + g + 8 * h < kvlen;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              float& v = sc[mt][2 * h + e];
+              v = valid ? v * sl2 : -INFINITY;
+              mb[e] = fmaxf(mb[e], v);
+            }
+          }
+        }
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const bool valid = kp0 + nt * 8 + 2 * tig + e < kvlen;
-          sc[nt][e] = valid ? sc[nt][e] * sl2 : -INFINITY;
-          sc[nt][2 + e] = valid ? sc[nt][2 + e] * sl2 : -INFINITY;
-          mb0 = fmaxf(mb0, sc[nt][e]);
-          mb1 = fmaxf(mb1, sc[nt][2 + e]);
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1) mb[e] = fmaxf(mb[e], __shfl_xor_sync(0xffffffffu, mb[e], off));
         }
-      }
-      mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, 1));
-      mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, 2));
-      mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, 1));
-      mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, 2));
-      const float mn0 = fmaxf(m0, mb0), mn1 = fmaxf(m1, mb1);
-      const float al0 = mn0 == -INFINITY ? 1.f : ex2f(m0 - mn0);
-      const float al1 = mn1 == -INFINITY ? 1.f : ex2f(m1 - mn1);
-      m0 = mn0;
-      m1 = mn1;
-      l0 *= al0;
-      l1 *= al1;
+        float mn[2], al[2];
 #pragma unroll
-      for (int t = 0; t < DT; ++t) {
-        o[t][0] *= al0;
-        o[t][1] *= al0;
-        o[t][2] *= al1;
-        o[t][3] *= al1;
-      }
-      // ---- P (rounded to the value dtype) as A fragments ----
-      uint32_t pa[KS > 0 ? kBlkM / 16 : 1][4];
-#pragma unroll
-      for (int ks = 0; ks < kBlkM / 16; ++ks) {
-        float p[2][4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int nt = 2 * ks + h;
-          p[h][0] = mn0 == -INFINITY ? 0.f : ex2f(sc[nt][0] - mn0);
-          p[h][1] = mn0 == -INFINITY ? 0.f : ex2f(sc[nt][1] - mn0);
-          p[h][2] = mn1 == -INFINITY ? 0.f : ex2f(sc[nt][2] - mn1);
-          p[h][3] = mn1 == -INFINITY ? 0.f : ex2f(sc[nt][3] - mn1);
-          l0 += p[h][0] + p[h][1];
-          l1 += p[h][2] + p[h][3];
+        for (int e = 0; e < 2; ++e) {
+          mn[e] = fmaxf(m[e], mb[e]);
+          al[e] = mn[e] == -INFINITY ? 1.f : ex2f(m[e] - mn[e]);
+          m[e] = mn[e];
+          l[e] *= al[e];
         }
-        pa[ks][0] = pack2<kF16>(p[0][0], p[0][1]);
-        pa[ks][1] = pack2<kF16>(p[0][2], p[0][3]);
-        pa[ks][2] = pack2<kF16>(p[1][0], p[1][1]);
-        pa[ks][3] = pack2<kF16>(p[1][2], p[1][3]);
-      }
-      // ---- O += P V ----
 #pragma unroll
-      for (int ks = 0; ks < kBlkM / 16; ++ks) {
-        const int row = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        for (int x = 0; x < MD; ++x) {
+          o[x][0] *= al[0];
+          o[x][1] *= al[1];
+          o[x][2] *= al[0];
+          o[x][3] *= al[1];
+        }
+        // ---- P^T (rounded to the value dtype) as B fragments via 8x8 transposes ----
+        uint32_t pb[2][2];
 #pragma unroll
-        for (int tp = 0; tp < DT / 2; ++tp) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(vbase + swz(row, 2 * tp + (lane >> 4)), b0, b1, b2, b3);
-          mma16816<kF16>(o[2 * tp], pa[ks], b0, b1);
-          mma16816<kF16>(o[2 * tp + 1], pa[ks], b2, b3);
+        for (int mt = 0; mt < 2; ++mt) {
+          float p[4];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int e = q4 & 1;
+            p[q4] = mn[e] == -INFINITY ? 0.f : ex2f(sc[mt][q4] - mn[e]);
+            l[e] += p[q4];
+          }
+          pb[mt][0] = movm_t(pack2<kF16>(p[0], p[1]));  // keys 0-7 of the m-tile
+          pb[mt][1] = movm_t(pack2<kF16>(p[2], p[3]));  // keys 8-15
+        }
+        // ---- O^T [D x 8 heads] += V^T P^T ----
+#pragma unroll
+        for (int md = 0; md < MD; ++md) {
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const int row = kk * 16 + (lane & 7) + (lane >> 4) * 8;
+            uint32_t af[4];
+            ldsm_x4_t(vbase + swz32(row, 2 * md + ((lane >> 3) & 1)), af[0], af[1], af[2], af[3]);
+            mma16816<kF16>(o[md], af, pb[kk][0], pb[kk][1]);
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    // quad-reduce l (each thread summed its own columns)
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    // ---- merge the two consumer warps in shared memory (reuses the ring) ----
-    named_bar(1, kConsumers * 32);
-    float* wbuf = reinterpret_cast<float*>(smem);  // [warps][16 rows][D + 2] : O (unnormalised), m, l
-    float* res = wbuf + kConsumers * 16 * (D + 2);  // [grp][D + 2]
+      if (t.n > 0 && t.j != t.n - 1) continue;
+      // ---- item done: warp-level finish (no shared memory) ----
+      float L[2], inv[2];
 #pragma unroll
-    for (int t = 0; t < DT; ++t) {
-      const int c = t * 8 + 2 * tig;
-      wbuf[(warp * 16 + g) * (D + 2) + c] = o[t][0];
-      wbuf[(warp * 16 + g) * (D + 2) + c + 1] = o[t][1];
-      wbuf[(warp * 16 + g + 8) * (D + 2) + c] = o[t][2];
-      wbuf[(warp * 16 + g + 8) * (D + 2) + c + 1] = o[t][3];
-    }
-    if (tig == 0) {
-      wbuf[(warp * 16 + g) * (D + 2) + D] = ok ? m0 : -INFINITY;
-      wbuf[(warp * 16 + g) * (D + 2) + D + 1] = ok ? l0 : 0.f;
-      wbuf[(warp * 16 + g + 8) * (D + 2) + D] = ok ? m1 : -INFINITY;
-      wbuf[(warp * 16 + g + 8) * (D + 2) + D + 1] = ok ? l1 : 0.f;
-    }
-    named_bar(1, kConsumers * 32);
-    const int tid = threadIdx.x;
-    for (int x = tid; x < grp * (D + 2); x += kConsumers * 32) {
-      const int r = x / (D + 2), d = x % (D + 2);
-      float mt = -INFINITY;
+      for (int e = 0; e < 2; ++e) {
+        L[e] = l[e];
 #pragma unroll
-      for (int w = 0; w < kConsumers; ++w) {
-        const float* row = wbuf + (w * 16 + r) * (D + 2);
-        if (row[D + 1] > 0.f) mt = fmaxf(mt, row[D]);
+        for (int off = 4; off < 32; off <<= 1) L[e] += __shfl_xor_sync(0xffffffffu, L[e], off);
+        inv[e] = L[e] > 0.f ? 1.f / L[e] : 0.f;
       }
-      float num = 0.f, den = 0.f;
+      if (nsplit == 1) {
 #pragma unroll
-      for (int w = 0; w < kConsumers; ++w) {
-        const float* row = wbuf + (w * 16 + r) * (D + 2);
-        if (row[D + 1] > 0.f) {
-          const float sc = ex2f(row[D] - mt);
-          den += row[D + 1] * sc;
-          if (d < D) num += row[d] * sc;
+        for (int e = 0; e < 2; ++e) {
+          const int hh = 2 * tig + e;
+          if (hh >= grp) continue;
+          const int hq = hk * grp + hh;
+          const int64_t row = (int64_t)b * a.Hq + hq;
+#pragma unroll
+          for (int md = 0; md < MD; ++md) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int d = md * 16 + g + 8 * h;
+              const float v = o[md][2 * h + e] * inv[e];
+              if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(v);
+              if (a.part_o) a.part_o[row * D + d] = v;
+            }
+          }
+          if (a.part_ml && g == 0) {
+            a.part_ml[row * 2] = m[e] * kLn2;
+            a.part_ml[row * 2 + 1] = L[e];
+          }
+        }
+        continue;
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int hh = 2 * tig + e;
+        if (hh >= grp) continue;
+        float* pr = ws.part + (((int64_t)b * a.Hq + hk * grp + hh) * ws.max_splits + split) * (D + 2);
+#pragma unroll
+        for (int md = 0; md < MD; ++md) {
+          pr[md * 16 + g] = o[md][e] * inv[e];
+          pr[md * 16 + g + 8] = o[md][2 + e] * inv[e];
+        }
+        if (g == 0) {
+          pr[D] = m[e] * kLn2;
+          pr[D + 1] = L[e];
         }
       }
-      float v;
-      if (d < D) v = den > 0.f ? num / den : 0.f;
-      else if (d == D) v = mt * kLn2;  // base-2 max -> base-e for the shared finish
-      else v = den;
-      res[x] = v;
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        last = atomicAdd(&ws.ticket[unit], 1) == nsplit - 1;
+        if (last) ws.ticket[unit] = 0;  // ready for the next call
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence();
+      for (int x = lane; x < grp * D; x += 32) {
+        const int gg = x / D, d = x % D;
+        const int64_t row = (int64_t)b * a.Hq + hk * grp + gg;
+        const float* pr = ws.part + row * ws.max_splits * (D + 2);
+        float mt = -INFINITY;
+        for (int sp = 0; sp < nsplit; ++sp)
+          if (__ldcg(pr + sp * (D + 2) + D + 1) > 0.f) mt = fmaxf(mt, __ldcg(pr + sp * (D + 2) + D));
+        float num = 0.f, den = 0.f;
+        for (int sp = 0; sp < nsplit; ++sp) {
+          const float lv = __ldcg(pr + sp * (D + 2) + D + 1);
+          if (lv > 0.f) {
+            const float w = lv * __expf(__ldcg(pr + sp * (D + 2) + D) - mt);
+            num = fmaf(w, __ldcg(pr + sp * (D + 2) + d), num);
+            den += w;
+          }
+        }
+        const float ov = den > 0.f ? num / den : 0.f;
+        if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + (hk * grp + gg) * a.o_stride[1] + d] = from_f<T>(ov);
+        if (a.part_o) a.part_o[row * D + d] = ov;
+        if (a.part_ml && d == 0) {
+          a.part_ml[row * 2] = mt;
+          a.part_ml[row * 2 + 1] = den;
+        }
+      }
     }
-    named_bar(1, kConsumers * 32);
-    decode_finish<T>(a, ws, nsplit, split, unit, b, hk, grp, res, tid, kConsumers * 32, 1, &s_last);
   }
   __syncwarp();
 }
@@ -319,20 +405,25 @@ __global__ void __launch_bounds__(kThreadsM, 3)
 template <int D, bool kF16>
 int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st) {
   CUtensorMap mk, mv;
-  if (!make_tmap_bhsd(&mk, a.k_cache, a.B, a.Hk, a.L, D, a.k_stride, 2, kBlkM) ||
-      !make_tmap_bhsd(&mv, a.v_cache, a.B, a.Hk, a.L, D, a.v_stride, 2, kBlkM)) {
+  if (!make_tmap_bhsd(&mk, a.k_cache, a.B, a.Hk, a.L, D, a.k_stride, 2, kSub) ||
+      !make_tmap_bhsd(&mv, a.v_cache, a.B, a.Hk, a.L, D, a.v_stride, 2, kSub)) {
     if (debug_enabled()) debug_log("decode: tensor map rejected, using the CUDA-core kernel");
     return TASFT_ERR_UNSUPPORTED;
   }
-  constexpr int kStage = 2 * (D / 64) * kBlkM * 128;
-  const int wbuf = (kConsumers * 16 + 16) * (D + 2) * 4;
-  const int ring = kStages * kStage;
-  const int smem = 1024 + (ring > wbuf ? ring : wbuf) + 2 * kStages * 8;
+  constexpr int kStage = 2 * (D / 64) * kSub * 128;
+  const int smem = 1024 + kStages * kStage + 2 * kStages * 8 + kStages * (int)sizeof(Tag);
   auto kern = bsa_decode_mma_kernel<D, kF16>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return TASFT_ERR_CUDA;
   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-  const int64_t grid = (int64_t)a.B * a.Hk * nsplit;
+  // persistent grid: every resident CTA slot, never more CTAs than work items
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreadsM, smem);
+  const int64_t items = (int64_t)a.B * a.Hk * nsplit;
+  int64_t grid = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
+  if (grid > items) grid = items;
   if (debug_enabled()) debug_log("decode_mma D=%d f16=%d grid=%lld smem=%d splits=%d", D, (int)kF16, (long long)grid, smem, nsplit);
   kern<<<(unsigned)grid, kThreadsM, smem, st>>>(mk, mv, a, ws, nsplit);
   count_launch();
@@ -344,7 +435,7 @@ int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaS
 int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st) {
   if (a.dtype != TASFT_BF16 && a.dtype != TASFT_F16) return TASFT_ERR_UNSUPPORTED;
   if (a.block != kBlkM || (a.D != 64 && a.D != 128)) return TASFT_ERR_UNSUPPORTED;
-  if (a.Hq / a.Hk > 16) return TASFT_ERR_UNSUPPORTED;
+  if (a.Hq / a.Hk > 8) return TASFT_ERR_UNSUPPORTED;  // q-heads of a group fill the MMA's N = 8
   // Q fragments are read as aligned 32-bit pairs
   if ((reinterpret_cast<uintptr_t>(a.q) & 3u) || (a.q_stride[0] & 1) || (a.q_stride[1] & 1)) return TASFT_ERR_UNSUPPORTED;
   const bool f16 = a.dtype == TASFT_F16;

@@ -77,7 +77,7 @@ extern "C" int tasft_bsa_decode_fwd_noalloc(const tasft_decode_args* ap, tasft_s
   DecodeWs ws{nullptr, nullptr, 0};
   if (nsplit > 1) {
     // same layout as tasft_decode_workspace_size: tickets (padded to 256 B), then partials
-    const int64_t tick = ((int64_t)a.B * a.Hk * 4 + 255) / 256 * 256;
+    const int64_t tick = ((int64_t)(a.B * a.Hk + 2) * 4 + 255) / 256 * 256;
     const int64_t need = tick + (int64_t)a.B * a.Hq * nsplit * (a.D + 2) * 4;
     if (need > kNoAllocScratchBytes) {
       if (debug_enabled())

@@ -67,8 +67,14 @@ __global__ void __launch_bounds__(kPoolThreads) gate_pool_project_kernel(tasft_g
     }
   }
   if (rg < RG) {
+    if constexpr (EPV % 4 == 0) {
 #pragma unroll
-    for (int e = 0; e < EPV; ++e) sm[rg * D + c * EPV + e] = acc[e];
+      for (int e = 0; e < EPV; e += 4)
+        *reinterpret_cast<float4*>(&sm[rg * D + c * EPV + e]) = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) sm[rg * D + c * EPV + e] = acc[e];
+    }
   }
   __syncthreads();
   float* mean = sm + RG * D;
@@ -84,16 +90,20 @@ __global__ void __launch_bounds__(kPoolThreads) gate_pool_project_kernel(tasft_g
   if (pooled) {
     for (int d = threadIdx.x; d < D; d += blockDim.x) pooled[prow * D + d] = mean[d];
   }
-  // projection: thread j < hid computes one output
+  // projection: one warp per hidden unit, lanes over D (coalesced weight rows)
   const int off = isq ? 0 : D;
-  for (int j = threadIdx.x; j < hid; j += blockDim.x) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int j = warp; j < hid; j += kPoolThreads / 32) {
     const float* w = a.w_in + (int64_t)j * 2 * D + off;
     float s = 0.f;
-    for (int d = 0; d < D; ++d) s = fmaf(w[d], mean[d], s);
-    if (isq) {
-      A[prow * hid + j] = s + a.b_in[j];
-    } else {
-      Ct[(((int64_t)b * H + h) * hid + j) * NB + blk] = s;
+    for (int d = lane; d < D; d += 32) s = fmaf(__ldg(w + d), mean[d], s);
+    s = warp_sum(s);
+    if (lane == 0) {
+      if (isq) {
+        A[prow * hid + j] = s + a.b_in[j];
+      } else {
+        Ct[(((int64_t)b * H + h) * hid + j) * NB + blk] = s;
+      }
     }
   }
 }

@@ -26,11 +26,16 @@ class DecodeWorkspace:
 
 
 def default_splits(B: int, Hk: int, mean_kept: float, sms: int = 148) -> int:
-    """CTAs per (sequence, kv-head): enough to fill ~4 CTAs per SM, >= 2 blocks each."""
+    """Splits per (sequence, kv-head) for the persistent decode kernel.
+
+    As many splits as keep the work items within the resident CTA slots (6 per SM), so
+    each CTA owns one item and no dynamic claiming is needed; at least two kept blocks
+    per split, at most 64 splits.
+    """
     units = max(1, B * Hk)
-    want = math.ceil(4 * sms / units)
-    cap = max(1, int(mean_kept // 2))
-    return max(1, min(want, cap, 64))
+    fit = max(1, (6 * sms) // units)
+    by_size = max(1, int(mean_kept // 2))
+    return max(1, min(fit, by_size, 64))
 
 
 def bsa_decode(

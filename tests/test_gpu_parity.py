@@ -262,6 +262,19 @@ class TestDecode:
                             T.KeptBlocks(idx.to(DEV), cnt.to(DEV)), num_splits=splits, workspace=ws)
         assert torch.equal(out, out2)
 
+    def test_dynamic_claiming_more_items_than_ctas(self):
+        """1536 work items > resident CTAs: items are claimed from the workspace counter,
+        which must be back at zero for the next call."""
+        q, kc, vc, kv_len, idx, cnt = _decode_case(64, 32, 8, 768, 128, torch.bfloat16, 0.5, 25)
+        ws = T.DecodeWorkspace(64, 32, 8, 128, 3, DEV)
+        kept = T.KeptBlocks(idx.to(DEV), cnt.to(DEV))
+        outs = [T.bsa_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), kv_len.to(DEV), kept, num_splits=3, workspace=ws)
+                for _ in range(3)]
+        assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+        ref = O.bsa_decode(q[:4], kc[:4], vc[:4], kv_len[:4], idx[:4], cnt[:4], 64)
+        assert_bf16_close(outs[0][:4], ref)
+        assert int(ws.buf[: 64 * 8 * 4 + 8].view(torch.int32).abs().sum()) == 0  # tickets and counters reset
+
     @pytest.mark.parametrize("dtype,D,grp", [(torch.float32, 64, 4), (torch.float16, 128, 7), (torch.bfloat16, 64, 1)])
     def test_dtypes(self, dtype, D, grp):
         q, kc, vc, kv_len, idx, cnt = _decode_case(3, 2 * grp, 2, 520, D, dtype, 0.5, 22)
