@@ -5,21 +5,28 @@
 // an fp32 online softmax, p cast to the value dtype before P.V, rows with nothing kept
 // give 0. Only the data movement and the arithmetic engine differ.
 //
-// CTA = one 128-row M tile made of two 64-row "slots" that share one kv-head:
+// Tile = one 128-row M tile made of two 64-row "slots" that share one kv-head:
 //   GQA (Hq/Hk >= 2): two q-heads of the group at the same q-block;
 //   MHA (Hq/Hk == 1): one head at two consecutive q-blocks.
-// The CTA walks the union of the two slots' kept lists; a per-entry 2-bit mask says
+// A tile walks the union of its two slots' kept lists; a per-entry 2-bit mask says
 // which slot keeps the block (the other slot's rows get p = 0). With lists at kv-head
 // granularity both slots keep the same blocks and nothing is wasted.
 //
-// Warp roles (192 threads, 2 CTAs per SM):
-//   warp 0     TMA producer: Q once, then K and V tiles of each kept block (2-stage ring)
-//   warp 1     MMA issuer:   S = Q K^T (SS, M128 N64) into a double-buffered TMEM tile,
-//                            O += P V (TS: P read from TMEM where it overwrote S)
-//   warps 2-5  softmax:      one thread per row; tcgen05.ld S, mask, online max with a
-//                            lazy O rescale (only when the max grows by > 2^8), p = 2^x,
-//                            tcgen05.st P (bf16) back into TMEM, epilogue O / l.
-// Every mbarrier wait is bounded (TASFT_DEVERR_TIMEOUT) so a broken pipeline returns.
+// Persistent CTAs (2 per SM, 192 threads) take tiles in a static stride over a
+// heavy-first order. Warp roles:
+//   warp 0     producer: builds the next tile's union list (double-buffered), loads Q
+//              once the previous tile's last S = Q K^T has run, and streams K/V tiles of
+//              every kept block through a 2-stage ring (TMA, 128B swizzle)
+//   warp 1     MMA issuer: S = Q K^T (SS, M128 N64) into a double-buffered TMEM tile,
+//              O += P V (TS: P read from TMEM where it overwrote S)
+//   warps 2-5  softmax: one thread per row; tcgen05.ld S, mask, online max with a lazy
+//              O rescale (only when the max grows by > 2^8), p = 2^x, tcgen05.st P (bf16)
+//              back into TMEM, epilogue O / l, which overlaps the next tile's loads.
+// Every mbarrier phase is indexed by a global block counter or by the CTA's tile counter,
+// and every wait is arranged so the waiter is at most one phase behind (a parity wait
+// cannot tell phase k from phase k + 2). Every wait is bounded (TASFT_DEVERR_TIMEOUT).
+#include <cstdlib>
+
 #include "tc.cuh"
 
 namespace tasft {
@@ -29,6 +36,7 @@ namespace {
 constexpr int kThreads = 192;
 constexpr int kBlk = 64;           // block size (tokens) handled by this kernel
 constexpr int kMaxNB = 1024;       // max blocks per sequence (S <= 65536)
+constexpr int kWords = kMaxNB / 32;
 constexpr uint32_t kTmemCols = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -39,6 +47,12 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+struct Work {
+  int b, hk, head[2], qbs[2];
+  int valid[2];
+  int n;  // union list length; -1 = no more tiles
+};
+
 template <int D>
 struct Smem {
   static constexpr int kChunks = D / 64;                  // 64-element (128 B) swizzle atoms along D
@@ -47,33 +61,29 @@ struct Smem {
   static constexpr int kStageBytes = 2 * kKVTileBytes;    // K + V
   static constexpr int kQOff = 0;
   static constexpr int kStageOff = kQOff + kQBytes;
-  static constexpr int kListOff = kStageOff + 2 * kStageBytes;
-  static constexpr int kBitmapOff = kListOff + kMaxNB * 4;
-  static constexpr int kBarOff = kBitmapOff + 2 * (kMaxNB / 32) * 4;
-  static constexpr int kNumBars = 11;
+  static constexpr int kListOff = kStageOff + 2 * kStageBytes;   // [2][kMaxNB] int32
+  static constexpr int kBitmapOff = kListOff + 2 * kMaxNB * 4;   // [2 slots][kWords] uint32
+  static constexpr int kWorkOff = kBitmapOff + 2 * kWords * 4;   // [2] Work
+  static constexpr int kBarOff = (kWorkOff + 2 * (int)sizeof(Work) + 7) / 8 * 8;
+  static constexpr int kNumBars = 18;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
-struct Work {
-  int b, hk, head[2], qbs[2];
-  bool valid[2];
-};
-
-__device__ __forceinline__ Work decode_work(const tasft_prefill_args& a, int NB) {
+// Tile id -> work. Ids run heavy (late) q-blocks first.
+__device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, int NB, int id) {
   const int grp = a.Hq / a.Hk;
   const int pairs = grp >= 2 ? (grp + 1) / 2 : 1;
   const int nbp = grp >= 2 ? NB : (NB + 1) / 2;
   const int inner = a.B * a.Hk * pairs;
-  const int id = blockIdx.x;
   const int qbo = id / inner;
   const int rem = id % inner;
   const int p = rem % pairs;
   Work w;
   w.hk = (rem / pairs) % a.Hk;
   w.b = rem / (pairs * a.Hk);
-  const int qslot = nbp - 1 - qbo;  // heavy (late) q-blocks first
+  const int qslot = nbp - 1 - qbo;
   for (int s = 0; s < 2; ++s) {
     if (grp >= 2) {
       w.head[s] = w.hk * grp + 2 * p + s;
@@ -85,7 +95,20 @@ __device__ __forceinline__ Work decode_work(const tasft_prefill_args& a, int NB)
       w.valid[s] = w.qbs[s] < NB;
     }
   }
+  w.n = 0;
   return w;
+}
+
+__device__ __forceinline__ int num_tiles(const tasft_prefill_args& a, int NB) {
+  const int grp = a.Hq / a.Hk;
+  const int pairs = grp >= 2 ? (grp + 1) / 2 : 1;
+  const int nbp = grp >= 2 ? NB : (NB + 1) / 2;
+  return a.B * a.Hk * pairs * nbp;
+}
+
+// Warp-wide bounded wait; every lane gets the same answer.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
 
 template <int D, bool kF16>
@@ -97,132 +120,174 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* sQ = smem + L::kQOff;
-  int32_t* list = reinterpret_cast<int32_t*>(smem + L::kListOff);
+  int32_t* lists = reinterpret_cast<int32_t*>(smem + L::kListOff);
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem + L::kBitmapOff);
+  Work* works = reinterpret_cast<Work*>(smem + L::kWorkOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* bar_q = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_ready = bars + 7;   // [2]
-  uint64_t* pv_done = bars + 9;
-  // Single-use barrier for the epilogue. pv_done cannot serve: when the softmax warps
-  // finish the last block, P.V of block n-2 may still run, and a parity wait cannot tell
-  // "phase n-2 pending" from "phase n-1 done".
-  uint64_t* o_final = bars + 10;
-  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);  // [0] tmem base, [1] list length, [2] abort
+  uint64_t* q_full = bars + 0;      // per tile: Q landed
+  uint64_t* q_empty = bars + 1;     // per tile: every S of the tile has run (Q reusable)
+  uint64_t* kv_full = bars + 2;     // [2] per block
+  uint64_t* kv_empty = bars + 4;    // [2] per block
+  uint64_t* s_full = bars + 6;      // [2] per block
+  uint64_t* p_ready = bars + 8;     // [2] per block (128 arrivals)
+  // P.V completion, alternating by block parity: a single barrier could be two phases
+  // ahead of a waiter at a tile boundary (P.V of block g-1 in flight while S(g) waits for
+  // g-2), which a parity wait cannot see.
+  uint64_t* pv_done = bars + 10;    // [2] per block
+  uint64_t* o_final = bars + 12;    // per tile: O complete
+  uint64_t* o_free = bars + 13;     // per tile: epilogue has read O (128 arrivals)
+  uint64_t* list_full = bars + 14;  // [2] per tile
+  uint64_t* list_empty = bars + 16; // [2] per tile (128 arrivals)
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);  // [0] tmem base
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const Work w = decode_work(a, NB);
+  const int tiles = num_tiles(a, NB);
   const int words = (NB + 31) / 32;
 
-  // ---------------- setup ----------------
   if (warp == 0 && lane == 0) {
-    mbar_init(bar_q, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i], 128);
+      mbar_init(&list_full[i], 1);
+      mbar_init(&list_empty[i], 128);
+      mbar_init(&pv_done[i], 1);
     }
-    mbar_init(pv_done, 1);
     mbar_init(o_final, 1);
+    mbar_init(o_free, 128);
     fence_barrier_init();
-    misc[2] = 0;
   }
   if (warp == 1) {
     tc::tmem_alloc(&misc[0], kTmemCols);
     tc::tmem_relinquish();
   }
-  for (int i = threadIdx.x; i < 2 * words; i += kThreads) bitmap[i] = 0;
-  __syncthreads();
-  // union of the two slots' kept lists as bitmaps
-  const int grp_m = a.Hq / a.Hm;
-  for (int s = 0; s < 2; ++s) {
-    if (!w.valid[s]) continue;
-    const int hm = w.head[s] / grp_m;
-    const int64_t lrow = ((int64_t)w.b * a.Hm + hm) * NB + w.qbs[s];
-    const int cnt = min(a.kept_cnt[lrow], NB);
-    const int32_t* idx = a.kept_idx + lrow * NB;
-    for (int t = threadIdx.x; t < cnt; t += kThreads) {
-      const int kb = idx[t];
-      if (kb < 0 || kb >= NB) {
-        set_err(a.err, TASFT_DEVERR_INDEX);
-        continue;
-      }
-      if (a.causal && kb > w.qbs[s]) continue;
-      atomicOr(&bitmap[s * words + (kb >> 5)], 1u << (kb & 31));
-    }
-  }
-  __syncthreads();
-  if (warp == 0) {
-    int n = 0;
-    for (int wd = 0; wd < words; ++wd) {
-      const uint32_t m0 = bitmap[wd], m1 = bitmap[words + wd];
-      const uint32_t bit = 1u << lane;
-      const bool any = ((m0 | m1) & bit) != 0;
-      const unsigned bal = __ballot_sync(0xffffffffu, any);
-      if (any) {
-        const int pos = n + __popc(bal & (bit - 1u));
-        const int slots = ((m0 & bit) ? 1 : 0) | ((m1 & bit) ? 2 : 0);
-        list[pos] = (wd * 32 + lane) | (slots << 16);
-      }
-      n += __popc(bal);
-    }
-    if (lane == 0) misc[1] = n;
-  }
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = misc[0];
-  const int n = misc[1];
-  const uint32_t tS0 = tmem;            // S buffers: columns [0,64) and [64,128)
-  const uint32_t tO = tmem + 128;       // O: columns [128, 128 + D)
+  const uint32_t tS0 = tmem;       // S buffers: columns [0,64) and [64,128)
+  const uint32_t tO = tmem + 128;  // O: columns [128, 128 + D)
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ================= producer =================
     if (lane == 0) {
       tc::prefetch_tmap(&tmq);
       tc::prefetch_tmap(&tmk);
       tc::prefetch_tmap(&tmv);
-      const int nvalid = (w.valid[0] ? 1 : 0) + (w.valid[1] ? 1 : 0);
-      mbar_arrive_expect_tx(bar_q, nvalid * L::kChunks * 64 * 128);
-      for (int s = 0; s < 2; ++s) {
-        if (!w.valid[s]) continue;
-        for (int c = 0; c < L::kChunks; ++c)
-          tc::tma_load_4d(sQ + c * 128 * 128 + s * 64 * 128, &tmq, c * 64, w.qbs[s] * kBlk, w.head[s], w.b, bar_q);
+    }
+    const int grp_m = a.Hq / a.Hm;
+    int gk = 0;  // global block counter (ring position)
+    bool ok = true;
+    for (int u = 0; ok; ++u) {
+      const int tile = blockIdx.x + u * gridDim.x;
+      const int lb = u & 1;
+      if (u >= 2 && !warp_wait(&list_empty[lb], ((u >> 1) - 1) & 1)) {
+        set_err(a.err, TASFT_DEVERR_TIMEOUT | (1 << (8 + 1)));
+        ok = false;
+        break;
       }
-      int issued = 0;
-      for (int j = 0; j < n; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1)) {
-          set_err(a.err, TASFT_DEVERR_TIMEOUT);
-          break;
+      Work w;
+      int* list = lists + lb * kMaxNB;
+      if (tile >= tiles) {
+        w.n = -1;
+      } else {
+        // ---- union of the two slots' kept lists (warp 0 only) ----
+        w = decode_tile(a, NB, tile);
+        for (int i = lane; i < 2 * words; i += 32) bitmap[(i / words) * kWords + i % words] = 0;
+        __syncwarp();
+        for (int s = 0; s < 2; ++s) {
+          if (!w.valid[s]) continue;
+          const int hm = w.head[s] / grp_m;
+          const int64_t lrow = ((int64_t)w.b * a.Hm + hm) * NB + w.qbs[s];
+          const int cnt = min(a.kept_cnt[lrow], NB);
+          const int32_t* idx = a.kept_idx + lrow * NB;
+          for (int t = lane; t < cnt; t += 32) {
+            const int kb = idx[t];
+            if (kb < 0 || kb >= NB) {
+              set_err(a.err, TASFT_DEVERR_INDEX);
+              continue;
+            }
+            if (a.causal && kb > w.qbs[s]) continue;
+            atomicOr(&bitmap[s * kWords + (kb >> 5)], 1u << (kb & 31));
+          }
         }
-        const int kb = list[j] & 0xffff;
-        uint8_t* sK = smem + L::kStageOff + st * L::kStageBytes;
-        uint8_t* sV = sK + L::kKVTileBytes;
-        mbar_arrive_expect_tx(&kv_full[st], L::kStageBytes);
-        for (int c = 0; c < L::kChunks; ++c) {
-          tc::tma_load_4d(sK + c * 64 * 128, &tmk, c * 64, kb * kBlk, w.hk, w.b, &kv_full[st]);
-          tc::tma_load_4d(sV + c * 64 * 128, &tmv, c * 64, kb * kBlk, w.hk, w.b, &kv_full[st]);
+        __syncwarp();
+        int n = 0;
+        for (int wd = 0; wd < words; ++wd) {
+          const uint32_t m0 = bitmap[wd], m1 = bitmap[kWords + wd];
+          const uint32_t bit = 1u << lane;
+          const bool any = ((m0 | m1) & bit) != 0;
+          const unsigned bal = __ballot_sync(0xffffffffu, any);
+          if (any) {
+            const int slots = ((m0 & bit) ? 1 : 0) | ((m1 & bit) ? 2 : 0);
+            list[n + __popc(bal & (bit - 1u))] = (wd * 32 + lane) | (slots << 16);
+          }
+          n += __popc(bal);
         }
-        ++issued;
+        w.n = n;
+        __syncwarp();
       }
-      // do not leave the CTA while copies into its shared memory are in flight
-      mbar_wait(bar_q, 0);
-      for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1);
+      if (lane == 0) {
+        works[lb] = w;
+        mbar_arrive(&list_full[lb]);  // release: the list and the work record
+      }
+      if (w.n < 0) break;
+      if (lane == 0) {
+        // ---- Q once the previous tile's S MMAs have run ----
+        if (u >= 1 && !mbar_wait(q_empty, (u - 1) & 1)) {
+          set_err(a.err, TASFT_DEVERR_TIMEOUT | (1 << (8 + 2)));
+          ok = false;
+        }
+        if (ok) {
+          const int nvalid = (w.valid[0] ? 1 : 0) + (w.valid[1] ? 1 : 0);
+          mbar_arrive_expect_tx(q_full, nvalid * L::kChunks * 64 * 128);
+          for (int s = 0; s < 2; ++s) {
+            if (!w.valid[s]) continue;
+            for (int c = 0; c < L::kChunks; ++c)
+              tc::tma_load_4d(sQ + c * 128 * 128 + s * 64 * 128, &tmq, c * 64, w.qbs[s] * kBlk, w.head[s], w.b,
+                              q_full);
+          }
+        }
+        // ---- K/V of every kept block ----
+        for (int j = 0; ok && j < w.n; ++j, ++gk) {
+          const int st = gk & 1;
+          if (gk >= 2 && !mbar_wait(&kv_empty[st], ((gk >> 1) - 1) & 1)) {
+            set_err(a.err, TASFT_DEVERR_TIMEOUT | (1 << (8 + 3)));
+            ok = false;
+            break;
+          }
+          const int kb = list[j] & 0xffff;
+          uint8_t* sK = smem + L::kStageOff + st * L::kStageBytes;
+          uint8_t* sV = sK + L::kKVTileBytes;
+          mbar_arrive_expect_tx(&kv_full[st], L::kStageBytes);
+          for (int c = 0; c < L::kChunks; ++c) {
+            tc::tma_load_4d(sK + c * 64 * 128, &tmk, c * 64, kb * kBlk, w.hk, w.b, &kv_full[st]);
+            tc::tma_load_4d(sV + c * 64 * 128, &tmv, c * 64, kb * kBlk, w.hk, w.b, &kv_full[st]);
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      gk = __shfl_sync(0xffffffffu, gk, 0);
+    }
+    // do not leave while copies into shared memory are in flight
+    if (lane == 0) {
+      for (int i = max(0, gk - 2); i < gk; ++i) mbar_wait(&kv_full[i & 1], (i >> 1) & 1);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ================= MMA issuer =================
     if (lane == 0) {
       constexpr uint32_t fmt = kF16 ? 0u : 1u;
       constexpr uint32_t idesc_s = tc::make_idesc(128, 64, fmt, false);
       constexpr uint32_t idesc_o = tc::make_idesc(128, D, fmt, true);
       const uint32_t q_addr = smem_u32(sQ);
-      bool ok = mbar_wait(bar_q, 0);
-      auto issue_s = [&](int j) {
-        const int st = j & 1;
+      int g = 0;  // global block counter
+      bool ok = true;
+      int where = 0;  // wait site that gave up (reported in the error word)
+      auto issue_s = [&](int gi) {
+        const int st = gi & 1;
         const uint32_t k_addr = smem_u32(smem + L::kStageOff + st * L::kStageBytes);
         const uint32_t dst = tS0 + st * 64;
 #pragma unroll
@@ -233,140 +298,163 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc::mma_commit(&s_full[st]);
       };
-      if (ok && n > 0) {
-        ok = mbar_wait(&kv_full[0], 0);
-        if (ok) {
-          tc::tc_fence_after();
-          issue_s(0);
-        }
-      }
-      for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n) {
-          ok = mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1);
-          if (ok && j >= 1) ok = mbar_wait(pv_done, (j - 1) & 1);
-          if (!ok) break;
-          tc::tc_fence_after();
-          issue_s(j + 1);
-        }
-        ok = mbar_wait(&p_ready[j & 1], (j >> 1) & 1);
-        if (!ok) break;
+      // S(gi) may overwrite S buffer gi & 1 once P.V of block gi - 2 has run
+      auto ready_s = [&](int gi) -> bool {
+        if (!mbar_wait(&kv_full[gi & 1], (gi >> 1) & 1)) { where = 4; return false; }
+        if (gi >= 2 && !mbar_wait(&pv_done[gi & 1], ((gi - 2) >> 1) & 1)) { where = 5; return false; }
         tc::tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + L::kStageOff + (j & 1) * L::kStageBytes + L::kKVTileBytes);
-        const uint32_t p_tmem = tS0 + (j & 1) * 64;
-#pragma unroll
-        for (int kk = 0; kk < kBlk / 16; ++kk) {
-          const uint64_t bd = tc::make_sdesc(v_addr + kk * 16 * 128, 64 * 128, 1024);
-          tc::mma_ts(tO, p_tmem + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        return true;
+      };
+      for (int u = 0; ok; ++u) {
+        const int lb = u & 1;
+        if (!mbar_wait(&list_full[lb], (u >> 1) & 1)) { where = 6; ok = false; break; }
+        const int n = works[lb].n;
+        if (n < 0) break;
+        if (!mbar_wait(q_full, u & 1)) { where = 7; ok = false; break; }
+        tc::tc_fence_after();
+        if (n > 0) {
+          ok = ready_s(g);
+          if (ok) issue_s(g);
         }
-        tc::mma_commit(&kv_empty[j & 1]);
-        tc::mma_commit(pv_done);
-        if (j == n - 1) tc::mma_commit(o_final);
+        if (n <= 1) tc::mma_commit(q_empty);  // no further S of this tile reads Q
+        for (int j = 0; ok && j < n; ++j) {
+          const int gi = g + j;
+          if (j + 1 < n) {
+            ok = ready_s(gi + 1);
+            if (!ok) break;
+            issue_s(gi + 1);
+            if (j + 2 == n) tc::mma_commit(q_empty);
+          }
+          if (!mbar_wait(&p_ready[gi & 1], (gi >> 1) & 1)) { where = 8; ok = false; break; }
+          // O is reused: the previous tile's epilogue must have read it
+          if (j == 0 && u >= 1 && !mbar_wait(o_free, (u - 1) & 1)) { where = 9; ok = false; break; }
+          tc::tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + L::kStageOff + (gi & 1) * L::kStageBytes + L::kKVTileBytes);
+          const uint32_t p_tmem = tS0 + (gi & 1) * 64;
+#pragma unroll
+          for (int kk = 0; kk < kBlk / 16; ++kk) {
+            const uint64_t bd = tc::make_sdesc(v_addr + kk * 16 * 128, 64 * 128, 1024);
+            tc::mma_ts(tO, p_tmem + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&kv_empty[gi & 1]);
+          tc::mma_commit(&pv_done[gi & 1]);
+        }
+        if (!ok) break;
+        if (n == 0 && u >= 1 && !mbar_wait(o_free, (u - 1) & 1)) { where = 10; ok = false; break; }
+        tc::mma_commit(o_final);
+        g += n;
       }
-      if (!ok) {
-        set_err(a.err, TASFT_DEVERR_TIMEOUT);
-        atomicExch(&misc[2], 1u);
-      }
+      if (!ok) set_err(a.err, TASFT_DEVERR_TIMEOUT | (1 << (8 + where)));
     }
   } else {
-    // ---------------- softmax + epilogue (warps 2..5) ----------------
+    // ================= softmax + epilogue (warps 2..5) =================
     const int quarter = warp & 3;            // TMEM lanes [32*quarter, 32*quarter + 32)
     const int r = quarter * 32 + lane;       // tile row
     const int slot = r >> 6;
-    const int qpos = w.qbs[slot] * kBlk + (r & 63);
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float sl2 = a.scale * kLog2e;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1))) { ok = false; break; }
-      tc::tc_fence_after();
-      const int entry = list[j];
-      const int kb = entry & 0xffff;
-      const bool active = w.valid[slot] && ((entry >> (16 + slot)) & 1);
-      uint32_t sraw[64];
-      tc::tmem_ld64_sync(tS0 + (j & 1) * 64 + lane_off, sraw);
-      const int kbase = kb * kBlk;
-      // keys valid for this row: < S, and <= qpos when causal
-      int lim = a.S - kbase;
-      if (a.causal) lim = min(lim, qpos - kbase + 1);
-      if (!active) lim = 0;
-      lim = max(0, min(lim, kBlk));
-      float x[64];
-      float mb = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        x[c] = __uint_as_float(sraw[c]) * sl2;
-        if (c < lim) mb = fmaxf(mb, x[c]);
-      }
-      const float m_new = fmaxf(m, mb);
-      bool need = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
-      if (m == -INFINITY) m = m_new;  // O row is still exactly zero: no rescale
-      const bool warp_need = __any_sync(0xffffffffu, need);
-      if (warp_need) {
-        // O must hold every earlier P.V before it is rescaled
-        if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1))) { ok = false; break; }
-        tc::tc_fence_after();
-        const float alpha = need ? ex2(m - m_new) : 1.0f;
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t o[32];
-          tc::tmem_ld32_sync(tO + c0 + lane_off, o);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tc::tmem_st32(tO + c0 + lane_off, o);
-        }
-        tc::tmem_wait_st();
-        if (need) {
-          l *= alpha;
-          m = m_new;
-        }
-      }
-      uint32_t pk[32];
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float p0 = (2 * c < lim) ? ex2(x[2 * c] - m) : 0.f;
-        const float p1 = (2 * c + 1 < lim) ? ex2(x[2 * c + 1] - m) : 0.f;
-        rs += p0 + p1;
-        pk[c] = kF16 ? tc::pack_f16x2(p0, p1) : tc::pack_bf16x2(p0, p1);
-      }
-      l += rs;
-      tc::tmem_st32(tS0 + (j & 1) * 64 + lane_off, pk);
-      tc::tmem_wait_st();
-      tc::tc_fence_before();
-      mbar_arrive(&p_ready[j & 1]);
-    }
-    if (ok && n > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(o_final, 0));
-      tc::tc_fence_after();
-    }
-    if (!ok) set_err(a.err, TASFT_DEVERR_TIMEOUT);
-    // epilogue: O / l -> global (rows >= S and invalid slots are not stored)
-    const bool store = w.valid[slot] && qpos < a.S;
     using T = typename std::conditional<kF16, __half, __nv_bfloat16>::type;
-    T* orow = reinterpret_cast<T*>(a.out) + w.b * a.o_stride[0] + (int64_t)w.head[slot] * a.o_stride[1] +
-              (int64_t)qpos * a.o_stride[2];
-    const float inv = (l > 0.f) ? 1.0f / l : 0.f;
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      uint32_t o[32];
-      if (n > 0) {
-        tc::tmem_ld32_sync(tO + c0 + lane_off, o);
-      } else {
+    int g = 0;
+    bool ok = true;
+    int where = 0;
+    for (int u = 0; ok; ++u) {
+      const int lb = u & 1;
+      if (!warp_wait(&list_full[lb], (u >> 1) & 1)) { where = 11; ok = false; break; }
+      const Work w = works[lb];
+      if (w.n < 0) break;
+      const int* list = lists + lb * kMaxNB;
+      const int qpos = w.qbs[slot] * kBlk + (r & 63);
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < w.n; ++j) {
+        const int gi = g + j;
+        if (!warp_wait(&s_full[gi & 1], (gi >> 1) & 1)) { where = 12; ok = false; break; }
+        tc::tc_fence_after();
+        const int entry = list[j];
+        const int kb = entry & 0xffff;
+        const bool active = w.valid[slot] && ((entry >> (16 + slot)) & 1);
+        uint32_t sraw[64];
+        tc::tmem_ld64_sync(tS0 + (gi & 1) * 64 + lane_off, sraw);
+        const int kbase = kb * kBlk;
+        // keys valid for this row: < S, and <= qpos when causal
+        int lim = a.S - kbase;
+        if (a.causal) lim = min(lim, qpos - kbase + 1);
+        if (!active) lim = 0;
+        lim = max(0, min(lim, kBlk));
+        float mb = -INFINITY;  // max of the raw (unscaled) scores; the scale is > 0
 #pragma unroll
-        for (int c = 0; c < 32; ++c) o[c] = 0u;
-      }
-      if (store) {
-        uint32_t pk[16];
+        for (int c = 0; c < 64; ++c)
+          if (c < lim) mb = fmaxf(mb, __uint_as_float(sraw[c]));
+        const float m_new = fmaxf(m, mb * sl2);
+        const bool need = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
+        if (m == -INFINITY) m = m_new;  // O row is still exactly zero: no rescale
+        if (__any_sync(0xffffffffu, need)) {
+          // O must hold every earlier P.V of this tile before it is rescaled
+          if (!warp_wait(&pv_done[(gi - 1) & 1], ((gi - 1) >> 1) & 1)) { where = 13; ok = false; break; }
+          tc::tc_fence_after();
+          const float alpha = need ? ex2(m - m_new) : 1.0f;
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t o[32];
+            tc::tmem_ld32_sync(tO + c0 + lane_off, o);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const float v0 = ok ? __uint_as_float(o[2 * c]) * inv : 0.f;
-          const float v1 = ok ? __uint_as_float(o[2 * c + 1]) * inv : 0.f;
-          pk[c] = kF16 ? tc::pack_f16x2(v0, v1) : tc::pack_bf16x2(v0, v1);
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tc::tmem_st32(tO + c0 + lane_off, o);
+          }
+          tc::tmem_wait_st();
+          if (need) {
+            l *= alpha;
+            m = m_new;
+          }
         }
-        uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+        uint32_t pk[32];
+        float rs = 0.f;
 #pragma unroll
-        for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = (2 * c < lim) ? ex2(fmaf(__uint_as_float(sraw[2 * c]), sl2, -m)) : 0.f;
+          const float p1 = (2 * c + 1 < lim) ? ex2(fmaf(__uint_as_float(sraw[2 * c + 1]), sl2, -m)) : 0.f;
+          rs += p0 + p1;
+          pk[c] = kF16 ? tc::pack_f16x2(p0, p1) : tc::pack_bf16x2(p0, p1);
+        }
+        l += rs;
+        tc::tmem_st32(tS0 + (gi & 1) * 64 + lane_off, pk);
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        mbar_arrive(&p_ready[gi & 1]);
       }
+      if (!ok) break;
+      if (!warp_wait(o_final, u & 1)) { where = 14; ok = false; break; }
+      tc::tc_fence_after();
+      // ---- epilogue: O / l -> global (rows >= S and invalid slots are not stored) ----
+      const bool store = w.valid[slot] && qpos < a.S;
+      T* orow = reinterpret_cast<T*>(a.out) + w.b * a.o_stride[0] + (int64_t)w.head[slot] * a.o_stride[1] +
+                (int64_t)qpos * a.o_stride[2];
+      const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        if (w.n > 0) {
+          tc::tmem_ld32_sync(tO + c0 + lane_off, o);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = 0u;
+        }
+        if (store) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float v0 = __uint_as_float(o[2 * c]) * inv;
+            const float v1 = __uint_as_float(o[2 * c + 1]) * inv;
+            pk[c] = kF16 ? tc::pack_f16x2(v0, v1) : tc::pack_bf16x2(v0, v1);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        }
+      }
+      tc::tc_fence_before();
+      mbar_arrive(o_free);
+      mbar_arrive(&list_empty[lb]);
+      g += w.n;
     }
+    if (!ok) set_err(a.err, TASFT_DEVERR_TIMEOUT | (1 << (8 + where)));
   }
   // ---------------- teardown ----------------
   __syncwarp();
@@ -389,11 +477,22 @@ int launch_tc(const tasft_prefill_args& a, cudaStream_t st) {
   const int grp = a.Hq / a.Hk;
   const int pairs = grp >= 2 ? (grp + 1) / 2 : 1;
   const int nbp = grp >= 2 ? NB : (NB + 1) / 2;
-  const int64_t grid = (int64_t)a.B * a.Hk * pairs * nbp;
+  const int64_t tiles = (int64_t)a.B * a.Hk * pairs * nbp;
   auto kern = bsa_prefill_tc_kernel<D, kF16>;
   const int smem = Smem<D>::kAlloc;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return TASFT_ERR_CUDA;
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t grid = 2LL * sms;  // persistent: two CTAs per SM
+  if (const char* cap = std::getenv("TASFT_PREFILL_GRID")) {  // debugging aid: fewer CTAs, more tiles each
+    const long long c = std::atoll(cap);
+    if (c > 0 && c < grid) grid = c;
+  }
+  if (grid > tiles) grid = tiles;
+  if (debug_enabled()) debug_log("prefill_tc D=%d tiles=%lld grid=%lld smem=%d", D, (long long)tiles, (long long)grid, smem);
   kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB);
   count_launch();
   return launch_status();

@@ -158,6 +158,17 @@ class TestPrefill:
         out = T.BlockSparseFlashAttention().forward(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV))
         assert_bf16_close(out, O.bsa_prefill_masked_dense(q, k, v, mask, 64))
 
+    @pytest.mark.parametrize("grid", ["1", "3"])
+    def test_persistent_many_tiles_per_cta(self, grid, monkeypatch):
+        """Cap the persistent grid so each CTA walks many tiles: the list/Q/O hand-offs
+        between consecutive tiles of one CTA are exercised at a small size."""
+        monkeypatch.setenv("TASFT_PREFILL_GRID", grid)
+        q, k, v, mask = _prefill_case(2, 8, 2, 1024, 128, torch.bfloat16, 0.4, seed=41)
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        out = T.BlockSparseFlashAttention().forward(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV), err=err)
+        assert int(err.item()) == 0
+        assert_bf16_close(out, O.bsa_prefill_masked_dense(q, k, v, mask, 64))
+
     def test_run_to_run_deterministic(self):
         q, k, v, mask = _prefill_case(2, 8, 2, 2048, 128, torch.bfloat16, 0.3, seed=33)
         kern = T.BlockSparseFlashAttention()
