@@ -15,8 +15,8 @@
 // Persistent CTAs (2 per SM, 192 threads) take tiles in a static stride over a
 // heavy-first order. Warp roles:
 //   warp 0     producer: builds the next tile's union list (double-buffered), loads Q
-//              once the previous tile's last S = Q K^T has run, and streams K/V tiles of
-//              every kept block through a 2-stage ring (TMA, 128B swizzle)
+//              once the previous tile's last S = Q K^T has run, and streams K and V tiles
+//              of every kept block through separate 2-stage rings (TMA, 128B swizzle)
 //   warp 1     MMA issuer: S = Q K^T (SS, M128 N64) into a double-buffered TMEM tile,
 //              O += P V (TS: P read from TMEM where it overwrote S)
 //   warps 2-5  softmax: one thread per row; tcgen05.ld S, mask, online max with a lazy
@@ -47,6 +47,52 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// ---- packed fp32 pair helpers (Blackwell f32x2 instructions) ----
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe, to take load off the MUFU unit. Range reduction
+// x = j + f with j = round(x) obtained by adding 1.5 * 2^23 (so j sits in the low
+// mantissa bits of t), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients
+// were fitted for this kernel (least squares on the relative error over [-1/2, 1/2],
+// max relative error 7.5e-5, well under the bf16 rounding applied to P afterwards);
+// 2^j is added to the exponent field. Inputs are clamped at -125 so the exponent stays
+// normal.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x = f2(fmaxf(lo_f(x), -125.f), fmaxf(hi_f(x), -125.f));
+  const uint64_t t = add2(x, f2(kRound, kRound));
+  const uint64_t r = add2(t, f2(-kRound, -kRound));
+  const uint64_t f = fma2(r, f2(-1.f, -1.f), x);
+  uint64_t p = fma2(f2(0.05517049878835678f, 0.05517049878835678f), f,
+                    f2(0.24260851740837097f, 0.24260851740837097f));
+  p = fma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
+  p = fma2(p, f, f2(0.9999282360076904f, 0.9999282360076904f));
+  const uint32_t plo = (uint32_t)p + ((uint32_t)t << 23);
+  const uint32_t phi = (uint32_t)(p >> 32) + ((uint32_t)(t >> 32) << 23);
+  return ((uint64_t)phi << 32) | plo;
+}
+
+constexpr int kMufuPairs = 18;  // pairs 0..17 on MUFU ex2, 18..31 by the polynomial
+
 struct Work {
   int b, hk, head[2], qbs[2];
   int valid[2];
@@ -58,14 +104,17 @@ struct Smem {
   static constexpr int kChunks = D / 64;                  // 64-element (128 B) swizzle atoms along D
   static constexpr int kQBytes = kChunks * 128 * 128;     // 128 rows x 128 B per chunk
   static constexpr int kKVTileBytes = kChunks * 64 * 128; // 64 rows x 128 B per chunk
-  static constexpr int kStageBytes = 2 * kKVTileBytes;    // K + V
+  // K and V sit in separate 2-stage rings: K(g) is released as soon as S(g) has run,
+  // long before P.V(g) releases V(g), so K loads run well ahead of their use.
+  static constexpr int kKOff = 0;                          // within the ring area
+  static constexpr int kVOff = 2 * kKVTileBytes;
   static constexpr int kQOff = 0;
   static constexpr int kStageOff = kQOff + kQBytes;
-  static constexpr int kListOff = kStageOff + 2 * kStageBytes;   // [2][kMaxNB] int32
+  static constexpr int kListOff = kStageOff + 4 * kKVTileBytes;  // [2][kMaxNB] int32
   static constexpr int kBitmapOff = kListOff + 2 * kMaxNB * 4;   // [2 slots][kWords] uint32
   static constexpr int kWorkOff = kBitmapOff + 2 * kWords * 4;   // [2] Work
   static constexpr int kBarOff = (kWorkOff + 2 * (int)sizeof(Work) + 7) / 8 * 8;
-  static constexpr int kNumBars = 18;
+  static constexpr int kNumBars = 22;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
@@ -126,8 +175,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars + 0;      // per tile: Q landed
   uint64_t* q_empty = bars + 1;     // per tile: every S of the tile has run (Q reusable)
-  uint64_t* kv_full = bars + 2;     // [2] per block
-  uint64_t* kv_empty = bars + 4;    // [2] per block
+  uint64_t* k_full = bars + 2;      // [2] per block
+  uint64_t* k_empty = bars + 4;     // [2] per block: S(g) has run
+  uint64_t* v_full = bars + 18;     // [2] per block
+  uint64_t* v_empty = bars + 20;    // [2] per block: P.V(g) has run
   uint64_t* s_full = bars + 6;      // [2] per block
   uint64_t* p_ready = bars + 8;     // [2] per block (128 arrivals)
   // P.V completion, alternating by block parity: a single barrier could be two phases
@@ -148,8 +199,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i], 128);
       mbar_init(&list_full[i], 1);
@@ -251,30 +304,41 @@ __global__ void __launch_bounds__(kThreads, 2)
                               q_full);
           }
         }
-        // ---- K/V of every kept block ----
-        for (int j = 0; ok && j < w.n; ++j, ++gk) {
-          const int st = gk & 1;
-          if (gk >= 2 && !mbar_wait(&kv_empty[st], ((gk >> 1) - 1) & 1)) {
-            set_err(a.err, TASFT_DEVERR_TIMEOUT | (1 << (8 + 3)));
-            ok = false;
-            break;
-          }
-          const int kb = list[j] & 0xffff;
-          uint8_t* sK = smem + L::kStageOff + st * L::kStageBytes;
-          uint8_t* sV = sK + L::kKVTileBytes;
-          mbar_arrive_expect_tx(&kv_full[st], L::kStageBytes);
-          for (int c = 0; c < L::kChunks; ++c) {
-            tc::tma_load_4d(sK + c * 64 * 128, &tmk, c * 64, kb * kBlk, w.hk, w.b, &kv_full[st]);
-            tc::tma_load_4d(sV + c * 64 * 128, &tmv, c * 64, kb * kBlk, w.hk, w.b, &kv_full[st]);
-          }
+        // ---- K(j) then V(j-1): the order the MMA warp consumes them ----
+        auto load_k = [&](int gi, int kb) -> bool {
+          const int st = gi & 1;
+          if (gi >= 2 && !mbar_wait(&k_empty[st], ((gi >> 1) - 1) & 1)) return false;
+          uint8_t* dst = smem + L::kStageOff + L::kKOff + st * L::kKVTileBytes;
+          mbar_arrive_expect_tx(&k_full[st], L::kKVTileBytes);
+          for (int c = 0; c < L::kChunks; ++c)
+            tc::tma_load_4d(dst + c * 64 * 128, &tmk, c * 64, kb * kBlk, w.hk, w.b, &k_full[st]);
+          return true;
+        };
+        auto load_v = [&](int gi, int kb) -> bool {
+          const int st = gi & 1;
+          if (gi >= 2 && !mbar_wait(&v_empty[st], ((gi >> 1) - 1) & 1)) return false;
+          uint8_t* dst = smem + L::kStageOff + L::kVOff + st * L::kKVTileBytes;
+          mbar_arrive_expect_tx(&v_full[st], L::kKVTileBytes);
+          for (int c = 0; c < L::kChunks; ++c)
+            tc::tma_load_4d(dst + c * 64 * 128, &tmv, c * 64, kb * kBlk, w.hk, w.b, &v_full[st]);
+          return true;
+        };
+        for (int j = 0; ok && j <= w.n && w.n > 0; ++j) {
+          if (j < w.n && !load_k(gk + j, list[j] & 0xffff)) ok = false;
+          if (ok && j >= 1 && !load_v(gk + j - 1, list[j - 1] & 0xffff)) ok = false;
         }
+        if (!ok) set_err(a.err, TASFT_DEVERR_TIMEOUT | (1 << (8 + 3)));
+        if (w.n > 0) gk += w.n;
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       gk = __shfl_sync(0xffffffffu, gk, 0);
     }
     // do not leave while copies into shared memory are in flight
     if (lane == 0) {
-      for (int i = max(0, gk - 2); i < gk; ++i) mbar_wait(&kv_full[i & 1], (i >> 1) & 1);
+      for (int i = max(0, gk - 2); i < gk; ++i) {
+        mbar_wait(&k_full[i & 1], (i >> 1) & 1);
+        mbar_wait(&v_full[i & 1], (i >> 1) & 1);
+      }
     }
   } else if (warp == 1) {
     // ================= MMA issuer =================
@@ -288,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       int where = 0;  // wait site that gave up (reported in the error word)
       auto issue_s = [&](int gi) {
         const int st = gi & 1;
-        const uint32_t k_addr = smem_u32(smem + L::kStageOff + st * L::kStageBytes);
+        const uint32_t k_addr = smem_u32(smem + L::kStageOff + L::kKOff + st * L::kKVTileBytes);
         const uint32_t dst = tS0 + st * 64;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -297,10 +361,11 @@ __global__ void __launch_bounds__(kThreads, 2)
           tc::mma_ss(dst, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
         tc::mma_commit(&s_full[st]);
+        tc::mma_commit(&k_empty[st]);
       };
       // S(gi) may overwrite S buffer gi & 1 once P.V of block gi - 2 has run
       auto ready_s = [&](int gi) -> bool {
-        if (!mbar_wait(&kv_full[gi & 1], (gi >> 1) & 1)) { where = 4; return false; }
+        if (!mbar_wait(&k_full[gi & 1], (gi >> 1) & 1)) { where = 4; return false; }
         if (gi >= 2 && !mbar_wait(&pv_done[gi & 1], ((gi - 2) >> 1) & 1)) { where = 5; return false; }
         tc::tc_fence_after();
         return true;
@@ -328,15 +393,16 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (!mbar_wait(&p_ready[gi & 1], (gi >> 1) & 1)) { where = 8; ok = false; break; }
           // O is reused: the previous tile's epilogue must have read it
           if (j == 0 && u >= 1 && !mbar_wait(o_free, (u - 1) & 1)) { where = 9; ok = false; break; }
+          if (!mbar_wait(&v_full[gi & 1], (gi >> 1) & 1)) { where = 15; ok = false; break; }
           tc::tc_fence_after();
-          const uint32_t v_addr = smem_u32(smem + L::kStageOff + (gi & 1) * L::kStageBytes + L::kKVTileBytes);
+          const uint32_t v_addr = smem_u32(smem + L::kStageOff + L::kVOff + (gi & 1) * L::kKVTileBytes);
           const uint32_t p_tmem = tS0 + (gi & 1) * 64;
 #pragma unroll
           for (int kk = 0; kk < kBlk / 16; ++kk) {
             const uint64_t bd = tc::make_sdesc(v_addr + kk * 16 * 128, 64 * 128, 1024);
             tc::mma_ts(tO, p_tmem + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
           }
-          tc::mma_commit(&kv_empty[gi & 1]);
+          tc::mma_commit(&v_empty[gi & 1]);
           tc::mma_commit(&pv_done[gi & 1]);
         }
         if (!ok) break;
@@ -380,10 +446,22 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (a.causal) lim = min(lim, qpos - kbase + 1);
         if (!active) lim = 0;
         lim = max(0, min(lim, kBlk));
-        float mb = -INFINITY;  // max of the raw (unscaled) scores; the scale is > 0
+        float sv[64];
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c < lim) mb = fmaxf(mb, __uint_as_float(sraw[c]));
+        for (int c = 0; c < 64; ++c) sv[c] = __uint_as_float(sraw[c]);
+        if (__any_sync(0xffffffffu, lim < kBlk)) {  // diagonal / ragged / inactive rows
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c >= lim) sv[c] = -INFINITY;
+        }
+        // max of the raw (unscaled) scores, four independent chains; the scale is > 0
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) mq[qd] = max3(mq[qd], sv[c + 2 * qd], sv[c + 2 * qd + 1]);
+        }
+        const float mb = max3(mq[0], mq[1], fmaxf(mq[2], mq[3]));
         const float m_new = fmaxf(m, mb * sl2);
         const bool need = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
         if (m == -INFINITY) m = m_new;  // O row is still exactly zero: no rescale
@@ -407,12 +485,22 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         uint32_t pk[32];
         float rs = 0.f;
+        if (m == -INFINITY) {  // nothing valid in this row yet: p = 0
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = (2 * c < lim) ? ex2(fmaf(__uint_as_float(sraw[2 * c]), sl2, -m)) : 0.f;
-          const float p1 = (2 * c + 1 < lim) ? ex2(fmaf(__uint_as_float(sraw[2 * c + 1]), sl2, -m)) : 0.f;
-          rs += p0 + p1;
-          pk[c] = kF16 ? tc::pack_f16x2(p0, p1) : tc::pack_bf16x2(p0, p1);
+          for (int c = 0; c < 32; ++c) pk[c] = 0u;
+        } else {
+          const uint64_t sc2 = f2(sl2, sl2), nm2 = f2(-m, -m);
+          uint64_t rs2 = 0;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const uint64_t x2 = fma2(f2(sv[2 * c], sv[2 * c + 1]), sc2, nm2);  // s * scale - m
+            uint64_t p2;
+            if (c < kMufuPairs) p2 = f2(ex2(lo_f(x2)), ex2(hi_f(x2)));
+            else p2 = exp2_poly2(x2);
+            rs2 = add2(rs2, p2);
+            pk[c] = kF16 ? tc::pack_f16x2(lo_f(p2), hi_f(p2)) : tc::pack_bf16x2(lo_f(p2), hi_f(p2));
+          }
+          rs = lo_f(rs2) + hi_f(rs2);
         }
         l += rs;
         tc::tmem_st32(tS0 + (gi & 1) * 64 + lane_off, pk);
