@@ -341,6 +341,27 @@ class TestTarget:
         ref = O.gate_target_from_qk(q, k, 64)
         assert (tgt.cpu() - ref.float()).abs().max().item() <= (1e-5 if dtype == torch.float32 else 2e-2)
 
+    @pytest.mark.parametrize("dtype,B,Hq,Hk,S,D", [
+        (torch.bfloat16, 1, 4, 1, 448, 64),     # odd NB: last M tile has one q-block
+        (torch.bfloat16, 2, 8, 2, 1000, 128),   # ragged S, GQA 4
+        (torch.bfloat16, 1, 3, 3, 640, 128),    # MHA: one head per unit
+        (torch.bfloat16, 1, 6, 2, 384, 64),     # GQA 3: a pair and a single head
+        (torch.float16, 1, 4, 2, 512, 128),
+        (torch.bfloat16, 1, 8, 2, 4096, 128),   # many units per CTA
+    ])
+    def test_tensor_core_block_max_matches_cuda_core(self, dtype, B, Hq, Hk, S, D):
+        g = torch.Generator(device=DEV).manual_seed(S + Hq)
+        q = torch.randn(B, Hq, S, D, device=DEV, generator=g).to(dtype)
+        k = torch.randn(B, Hk, S, D, device=DEV, generator=g).to(dtype)
+        t_tc, bm_tc = T.gate_target_from_qk(q, k, 64, return_block_max=True)
+        t_ref, bm_ref = T.gate_target_from_qk(q, k, 64, return_block_max=True, force_simt=True)
+        torch.cuda.synchronize()
+        inf = torch.isinf(bm_ref)
+        assert torch.equal(inf, torch.isinf(bm_tc))
+        # fp32 accumulation in another order; bf16-emulated maxima may land one bf16 ulp apart
+        assert (bm_tc[~inf] - bm_ref[~inf]).abs().max().item() <= 1e-2 * bm_ref[~inf].abs().max().item()
+        assert (t_tc - t_ref).abs().max().item() <= 2e-2 * t_ref.max().item() + 1e-6
+
     def test_alternate_target(self):
         g = torch.Generator().manual_seed(5)
         q = torch.randn(1, 2, 256, 64, generator=g) * 3
