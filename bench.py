@@ -335,6 +335,23 @@ def run_ours(args):
                               "traffic": traffic.get("gate_pool"),
                               "algorithmic": f"{gbytes / 1e6:.1f} MB per step (|Q| + |K|)"}}
 
+    # ---------------- training gate target (tensor-core bound: causal Q K^T tiles) ----------------
+    def tstep():
+        T.gate_target_from_qk(q, k, CFG["block"])
+
+    t_tgt = time_steps(tstep, args.steps, args.warmup, flush, ws)
+    ms_t = statistics.mean(t_tgt)
+    nb = CFG["S"] // CFG["block"]
+    tflop = nb * (nb + 1) // 2 * 2 * CFG["block"] * CFG["block"] * CFG["D"] * CFG["B"] * CFG["Hq"]
+    t_ach = tflop / (ms_t * 1e-3) / 1e12
+    target_info = {"ms_per_step": round(ms_t, 4), "kernels": "target_tc_kernel + target_softmax_kernel",
+                   "config": "BASELINE configs[4]: gate target at the prefill shape (B=4, Hq=32, Hk=8, S=4096, D=128)",
+                   "roofline": {"bound": "tensor", "achieved": round(t_ach, 2), "peak": peaks["bf16_tflops"],
+                                "unit": "TFLOP/s", "frac": round(t_ach / peaks["bf16_tflops"], 4),
+                                "traffic": traffic.get("target"), "peak_src": f"bf16 burst, {peaks['src']}",
+                                "algorithmic": f"{tflop / 1e9:.1f} GFLOP per step (causal 64x64 tiles x 2*64*64*128 "
+                                               "x B x Hq)"}}
+
     # ---------------- e2e through the public API with host buffers ----------------
     qh = q.cpu().pin_memory()
     kh = k.cpu().pin_memory()
@@ -404,6 +421,7 @@ def run_ours(args):
                     "api": "tasft_b200.BlockSparseFlashAttention.forward(q, k, v, bool mask) from pinned host"},
             "decode": decode,
             "gate": gate_info,
+            "gate_target": target_info,
             "gpu_launches": launches * args.steps,
             "gpu_launches_per_step": launches,
             "clocks": clk.summary(),
@@ -439,7 +457,7 @@ def run_only(args):
                 with torch.no_grad():
                     gate(q, k)
             else:
-                T.gate_target_from_qk(q[:1], k[:1], CFG["block"])
+                T.gate_target_from_qk(q, k, CFG["block"])
     torch.cuda.synchronize()
     print(f"{args.only}: {args.steps} launches ok")
 
