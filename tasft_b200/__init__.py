@@ -17,6 +17,7 @@ from tasft_b200.block_sparse_fa import (
 from tasft_b200.decode import DecodeWorkspace, bsa_decode, decode_combine
 from tasft_b200.exceptions import KernelError, NaNDetectedError, TASFTError, ValidationError
 from tasft_b200.patch import patch, unpatch
+from tasft_b200 import shards
 from tasft_b200.training import TASFTObjective, gate_losses, gate_objective, gate_target_from_qk
 from tasft_b200.types import VALID_BLOCK_SIZES, KeptBlocks
 
@@ -42,6 +43,7 @@ __all__ = [
     "gate_target_from_qk",
     "mask_to_kept",
     "patch",
+    "shards",
     "threshold_scores",
     "unpatch",
 ]

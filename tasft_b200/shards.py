@@ -1,0 +1,113 @@
+"""Multi-GPU sharding of the sparse-attention path: one process per GPU, ``torch.distributed``.
+
+Prefill, the gate and batched decode split into independent units (sequence, kv-head):
+every unit reads only its own Q/K/V slice, so ranks share nothing and exchange nothing.
+``assign_units`` balances units over ranks by their kept-block counts (longest first).
+
+Long-context decode (one sequence, few kv-heads, a KV cache too large or too slow for one
+GPU) is the one path with an exchange. Rank r holds a contiguous range of KV blocks
+(``block_range``) of every kv-head. It decodes over the kept blocks that fall in its range
+and writes, per q-head, its normalised output with (max, sum). Then the partials of all
+ranks are all-gathered (NCCL over NVLink; 4*(D+2) bytes per q-head per rank) and merged
+locally by the log-sum-exp combine kernel. The reference has no sparse decode at all; the
+per-rank kernel follows the single-GPU decode's contract.
+"""
+from __future__ import annotations
+
+import heapq
+
+import torch
+
+from tasft_b200.types import KeptBlocks
+
+
+def assign_units(weights, world: int) -> list[list[int]]:
+    """Longest-processing-time assignment of unit ids to ``world`` ranks.
+
+    ``weights[i]`` is unit i's work (its kept-block count). Returns one ascending id list
+    per rank; ties go to the lower rank, so every rank computes the same answer.
+    """
+    if world <= 0:
+        raise ValueError("world must be positive")
+    w = [float(x) for x in (weights.tolist() if isinstance(weights, torch.Tensor) else weights)]
+    order = sorted(range(len(w)), key=lambda i: (-w[i], i))
+    heap = [(0.0, r) for r in range(world)]
+    out: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        load, r = heapq.heappop(heap)
+        out[r].append(i)
+        heapq.heappush(heap, (load + w[i], r))
+    return [sorted(x) for x in out]
+
+
+def block_range(nb: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous KV-block range ``[lo, hi)`` of ``rank`` when ``nb`` blocks split over ``world``."""
+    base, extra = divmod(nb, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def local_kept(kept: KeptBlocks, lo: int, hi: int) -> KeptBlocks:
+    """Decode lists ``[B, Hk, NBmax]`` restricted to blocks in ``[lo, hi)`` and rebased to
+    the local cache slab (block ``lo`` becomes 0), ascending order kept, padded with -1."""
+    idx, cnt = kept.idx, kept.cnt
+    pos = torch.arange(idx.shape[-1], device=idx.device)
+    inside = (pos < cnt.unsqueeze(-1)) & (idx >= lo) & (idx < hi)
+    big = torch.iinfo(torch.int32).max
+    key = torch.where(inside, idx - lo, torch.full_like(idx, big))
+    key = torch.sort(key, dim=-1).values  # lists are ascending, so this only compacts
+    key = torch.where(key == big, torch.full_like(key, -1), key)
+    return KeptBlocks(key.to(torch.int32).contiguous(), inside.sum(-1).to(torch.int32).contiguous())
+
+
+def local_kv_len(kv_len: torch.Tensor, lo: int, hi: int, block: int) -> torch.Tensor:
+    """Valid tokens of the local slab ``[lo*block, hi*block)`` for each sequence."""
+    return (kv_len.to(torch.int64) - lo * block).clamp(0, (hi - lo) * block).to(torch.int32)
+
+
+def gather_partials(part_o: torch.Tensor, part_ml: torch.Tensor, group=None):
+    """All-gather ``o [B,Hq,D]`` and ``ml [B,Hq,2]`` (fp32) from every rank of ``group``:
+    returns ``[G,B,Hq,D]`` and ``[G,B,Hq,2]`` in rank order."""
+    import torch.distributed as dist  # noqa: PLC0415
+
+    g = dist.get_world_size(group)
+    po = torch.empty((g, *part_o.shape), dtype=part_o.dtype, device=part_o.device)
+    pm = torch.empty((g, *part_ml.shape), dtype=part_ml.dtype, device=part_ml.device)
+    # into views of one preallocated tensor per kind (works on NCCL and on gloo)
+    dist.all_gather(list(po.unbind(0)), part_o.contiguous(), group=group)
+    dist.all_gather(list(pm.unbind(0)), part_ml.contiguous(), group=group)
+    return po, pm
+
+
+def long_context_decode(
+    q: torch.Tensor,
+    k_local: torch.Tensor,
+    v_local: torch.Tensor,
+    kv_len: torch.Tensor,
+    kept: KeptBlocks,
+    block_lo: int,
+    group=None,
+    block: int = 64,
+    num_splits: int = 0,
+) -> torch.Tensor:
+    """Sparse decode of a KV cache split by position over the ranks of ``group``.
+
+    ``k_local``/``v_local`` ``[B,Hk,Lloc,D]`` hold global blocks ``[block_lo, block_lo +
+    Lloc/block)``; ``kept`` and ``kv_len`` are the global lists and lengths (the same on
+    every rank). Every rank returns the full ``[B,Hq,D]`` result.
+    """
+    from tasft_b200.decode import bsa_decode, decode_combine  # noqa: PLC0415
+
+    B, Hq, D = q.shape
+    nloc = k_local.shape[2] // block
+    lo, hi = block_lo, block_lo + nloc
+    kl = local_kept(kept, lo, hi)
+    po = torch.empty(B, Hq, D, dtype=torch.float32, device=q.device)
+    pm = torch.empty(B, Hq, 2, dtype=torch.float32, device=q.device)
+    bsa_decode(q, k_local, v_local, local_kv_len(kv_len, lo, hi, block), kl, block,
+               num_splits=num_splits, partials=(po, pm))
+    ao, am = gather_partials(po, pm, group)
+    return decode_combine(ao, am, q.dtype)
+
+
+__all__ = ["assign_units", "block_range", "gather_partials", "local_kept", "local_kv_len", "long_context_decode"]

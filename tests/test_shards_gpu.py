@@ -1,0 +1,87 @@
+"""Split-KV long-context decode on the GPU: per-rank slabs through the CUDA decode with
+partials, merged by the combine kernel, against the unsplit decode (one GPU emulates the
+ranks), and the real exchange over NCCL when two GPUs are present."""
+from __future__ import annotations
+
+import math
+import os
+import socket
+
+import pytest
+import torch
+
+import tasft_b200 as T
+from tasft_b200 import masks as M
+from tasft_b200 import shards as SH
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _inputs(dev, B=1, Hq=28, Hk=4, Lc=8192, D=128, density=0.1, seed=11):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, Hq, D, device=dev, dtype=torch.bfloat16, generator=g)
+    kc = torch.randn(B, Hk, Lc, D, device=dev, dtype=torch.bfloat16, generator=g)
+    vc = torch.randn(B, Hk, Lc, D, device=dev, dtype=torch.bfloat16, generator=g)
+    kv_len = torch.full((B,), Lc - 37, dtype=torch.int32, device=dev)
+    nb = math.ceil(Lc / 64)
+    mask = M.decode_mask(torch.rand(B, Hk, nb, device=dev, generator=g), (kv_len + 63) // 64, density, nb)
+    idx, cnt = M.lists_from_mask(mask)
+    return q, kc, vc, kv_len, T.KeptBlocks(idx, cnt)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_emulated_ranks_match_unsplit(world):
+    q, kc, vc, kv_len, kept = _inputs(DEV)
+    ref = T.bsa_decode(q, kc, vc, kv_len, kept, 64).float()
+    nb = kc.shape[2] // 64
+    pos, pms = [], []
+    for r in range(world):
+        lo, hi = SH.block_range(nb, r, world)
+        kl = SH.local_kept(kept, lo, hi)
+        po = torch.empty(q.shape, dtype=torch.float32, device=DEV)
+        pm = torch.empty(*q.shape[:2], 2, dtype=torch.float32, device=DEV)
+        T.bsa_decode(q, kc[:, :, lo * 64 : hi * 64].contiguous(), vc[:, :, lo * 64 : hi * 64].contiguous(),
+                     SH.local_kv_len(kv_len, lo, hi, 64), kl, 64, partials=(po, pm))
+        pos.append(po)
+        pms.append(pm)
+    out = T.decode_combine(torch.stack(pos), torch.stack(pms), torch.bfloat16).float()
+    # bf16 output tolerance of the suite
+    assert (out - ref).abs().max().item() <= 2e-2
+
+
+def _rank(rank, world, port, res):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist  # noqa: PLC0415
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        q, kc, vc, kv_len, kept = _inputs(dev)
+        lo, hi = SH.block_range(kc.shape[2] // 64, rank, world)
+        out = SH.long_context_decode(q, kc[:, :, lo * 64 : hi * 64].contiguous(),
+                                     vc[:, :, lo * 64 : hi * 64].contiguous(), kv_len, kept, lo)
+        ref = T.bsa_decode(q, kc, vc, kv_len, kept, 64)
+        res.put((rank, (out.float() - ref.float()).abs().max().item()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_two_ranks_match_unsplit():
+    import torch.multiprocessing as mp  # noqa: PLC0415
+
+    ctx = mp.get_context("spawn")
+    res = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, res)) for r in range(2)]
+    for p in procs:
+        p.start()
+    errs = dict(res.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert max(errs.values()) <= 2e-2
