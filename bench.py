@@ -39,6 +39,7 @@ METRIC = "prefill effective TFLOP/s + decode tok/s, Llama-3-8B attn @80% sparsit
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 CFG = dict(B=4, Hq=32, Hk=8, S=4096, D=128, block=64, density=0.2)
 DEC = dict(B=64, Hq=32, Hk=8, L=8192, D=128, block=64, density=0.2)
+LONG = dict(B=1, Hq=28, Hk=4, L=32768, D=128, block=64, density=0.1)
 
 
 def load_peaks():
@@ -399,6 +400,36 @@ def run_ours(args):
                            "peak_src": peaks["src"], "kernel": "bsa_decode_mma_kernel",
                            "algorithmic": f"{dbytes / 1e6:.1f} MB per launch (kept K+V blocks + q + out)"}}
 
+    # ---------------- long-context decode: cache split by position over ranks ----------------
+    from tasft_b200 import masks as M  # noqa: PLC0415
+    from tasft_b200 import shards as SH  # noqa: PLC0415
+
+    lc = LONG
+    g = torch.Generator(device=dev).manual_seed(1234 + 4)  # same cache and lists on every rank
+    ql = torch.randn(lc["B"], lc["Hq"], lc["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    nbl = lc["L"] // lc["block"]
+    lo, hi = SH.block_range(nbl, rank, ws)
+    kl_loc = torch.randn(lc["B"], lc["Hk"], (hi - lo) * lc["block"], lc["D"], device=dev, dtype=torch.bfloat16,
+                         generator=g)
+    vl_loc = torch.randn_like(kl_loc)
+    kvl = torch.full((lc["B"],), lc["L"], dtype=torch.int32, device=dev)
+    lmask = M.decode_mask(torch.rand(lc["B"], lc["Hk"], nbl, device=dev, generator=g), (kvl + 63) // 64,
+                          lc["density"], nbl)
+    lkept = T.KeptBlocks(*M.lists_from_mask(lmask))
+    if ws > 1:
+        lstep = lambda: SH.long_context_decode(ql, kl_loc, vl_loc, kvl, lkept, lo)  # noqa: E731
+    else:
+        lstep = lambda: T.bsa_decode(ql, kl_loc, vl_loc, kvl, lkept, lc["block"])  # noqa: E731
+    t_long = time_steps(lstep, args.steps, args.warmup, flush, ws)
+    ms_l = max_over_ranks(statistics.mean(t_long), ws)
+    long_decode = {"config": "BASELINE configs[3] decode: B=1, Hq=28, Hk=4, KV=32768, D=128, 90% block sparsity "
+                             f"({int(lkept.cnt.float().mean().item())} of {nbl} blocks kept per kv-head)",
+                   "split": f"KV positions over {ws} rank(s); partials all-gathered + log-sum-exp combine"
+                            if ws > 1 else "one GPU",
+                   "scaling": "strong", "ms_per_token": round(ms_l, 4),
+                   "tok_s": round(lc["B"] / (ms_l * 1e-3), 1)}
+    del kl_loc, vl_loc
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         cpu = cpu_prefill_sample(budget_s=args.cpu_budget)
@@ -422,6 +453,7 @@ def run_ours(args):
             "decode": decode,
             "gate": gate_info,
             "gate_target": target_info,
+            "long_decode": long_decode,
             "gpu_launches": launches * args.steps,
             "gpu_launches_per_step": launches,
             "clocks": clk.summary(),

@@ -361,7 +361,8 @@ extern "C" int tasft_bsa_decode_fwd(const tasft_decode_args* ap, tasft_stream_t 
   if (nsplit <= 0) {
     const int units = a.B * a.Hk;
     nsplit = (6 * 148) / units;  // items within the resident CTA slots
-    const int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
+    int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
+    if (cap > 16) cap = 16;  // the last split merges all partials with one warp
     if (nsplit > cap) nsplit = cap;
     if (nsplit < 1) nsplit = 1;
   }
@@ -427,7 +428,8 @@ int decode_pick_splits(const tasft_decode_args& a) {
   if (nsplit <= 0) {
     const int units = a.B * a.Hk;
     nsplit = (6 * 148) / units;  // items within the resident CTA slots
-    const int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
+    int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
+    if (cap > 16) cap = 16;  // the last split merges all partials with one warp
     if (nsplit > cap) nsplit = cap;
     if (nsplit < 1) nsplit = 1;
   }

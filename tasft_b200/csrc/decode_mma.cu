@@ -373,26 +373,59 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
       last = __shfl_sync(0xffffffffu, last, 0);
       if (!last) continue;
       __threadfence();
-      for (int x = lane; x < grp * D; x += 32) {
-        const int gg = x / D, d = x % D;
+      // merge, per q-head row: the max over the splits (lanes over splits), then chunks
+      // of 16 splits whose partial rows are all loaded before any is used (independent
+      // 8-byte loads, lane -> d = 2 lane + 64 i), weighted by shuffle
+      for (int gg = 0; gg < grp; ++gg) {
         const int64_t row = (int64_t)b * a.Hq + hk * grp + gg;
         const float* pr = ws.part + row * ws.max_splits * (D + 2);
         float mt = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp)
+        for (int sp = lane; sp < nsplit; sp += 32)
           if (__ldcg(pr + sp * (D + 2) + D + 1) > 0.f) mt = fmaxf(mt, __ldcg(pr + sp * (D + 2) + D));
-        float num = 0.f, den = 0.f;
-        for (int sp = 0; sp < nsplit; ++sp) {
-          const float lv = __ldcg(pr + sp * (D + 2) + D + 1);
-          if (lv > 0.f) {
-            const float w = lv * __expf(__ldcg(pr + sp * (D + 2) + D) - mt);
-            num = fmaf(w, __ldcg(pr + sp * (D + 2) + d), num);
-            den += w;
+        mt = warp_max(mt);
+        constexpr int DP = D / 64;  // float2 per lane per split
+        float2 num[DP];
+#pragma unroll
+        for (int i = 0; i < DP; ++i) num[i] = make_float2(0.f, 0.f);
+        float den = 0.f;
+        for (int base = 0; base < nsplit; base += 16) {
+          const int nb = min(16, nsplit - base);
+          float w = 0.f;  // lane j (< nb) holds split base + j's weight
+          if (lane < nb) {
+            const float lv = __ldcg(pr + (base + lane) * (D + 2) + D + 1);
+            if (lv > 0.f) w = lv * __expf(__ldcg(pr + (base + lane) * (D + 2) + D) - mt);
+          }
+          den += w;
+          float2 v[16][DP];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+#pragma unroll
+            for (int i = 0; i < DP; ++i)
+              v[j][i] = j < nb ? __ldcg(reinterpret_cast<const float2*>(pr + (base + j) * (D + 2) + i * 64) + lane)
+                               : make_float2(0.f, 0.f);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float wj = __shfl_sync(0xffffffffu, w, j);
+#pragma unroll
+            for (int i = 0; i < DP; ++i) {
+              num[i].x = fmaf(wj, v[j][i].x, num[i].x);
+              num[i].y = fmaf(wj, v[j][i].y, num[i].y);
+            }
           }
         }
-        const float ov = den > 0.f ? num / den : 0.f;
-        if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + (hk * grp + gg) * a.o_stride[1] + d] = from_f<T>(ov);
-        if (a.part_o) a.part_o[row * D + d] = ov;
-        if (a.part_ml && d == 0) {
+        den = warp_sum(den);
+        const float inv_den = den > 0.f ? 1.f / den : 0.f;
+#pragma unroll
+        for (int i = 0; i < DP; ++i) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int d = i * 64 + 2 * lane + h;
+            const float ov = (h ? num[i].y : num[i].x) * inv_den;
+            if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + (hk * grp + gg) * a.o_stride[1] + d] = from_f<T>(ov);
+            if (a.part_o) a.part_o[row * D + d] = ov;
+          }
+        }
+        if (a.part_ml && lane == 0) {
           a.part_ml[row * 2] = mt;
           a.part_ml[row * 2 + 1] = den;
         }

@@ -30,12 +30,13 @@ def default_splits(B: int, Hk: int, mean_kept: float, sms: int = 148) -> int:
 
     As many splits as keep the work items within the resident CTA slots (6 per SM), so
     each CTA owns one item and no dynamic claiming is needed; at least two kept blocks
-    per split, at most 64 splits.
+    per split, at most 16 splits (the last split of a unit merges all partials with one
+    warp, and past 16 that merge costs more than the extra parallelism gains).
     """
     units = max(1, B * Hk)
     fit = max(1, (6 * sms) // units)
     by_size = max(1, int(mean_kept // 2))
-    return max(1, min(fit, by_size, 64))
+    return max(1, min(fit, by_size, 16))
 
 
 def bsa_decode(
@@ -74,7 +75,7 @@ def bsa_decode(
     ws_ptr, ws_bytes = None, 0
     if num_splits != 1:
         if workspace is None:
-            ms = num_splits if num_splits > 0 else 64
+            ms = num_splits if num_splits > 0 else 16
             workspace = DecodeWorkspace(B, Hq, Hk, D, ms, q.device)
         ws_ptr, ws_bytes = workspace.buf.data_ptr(), workspace.bytes
         if num_splits <= 0:
