@@ -46,7 +46,7 @@
 extern "C" {
 #endif
 
-#define TASFT_ABI_VERSION 1
+#define TASFT_ABI_VERSION 2
 
 /* status codes (host-side, returned) */
 #define TASFT_OK                  0
@@ -96,8 +96,10 @@ typedef struct {
   int64_t workspace_bytes;
 } tasft_gate_args;
 
+/* Workspace of tasft_gate_mask_build: the projected block rows plus the fp32 block means
+ * (ABI 2 added `D`). */
 TASFT_API int64_t tasft_gate_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t Sq, int32_t Sk,
-                                  int32_t block, int32_t hidden);
+                                  int32_t block, int32_t hidden, int32_t D);
 TASFT_API int tasft_gate_mask_build(const tasft_gate_args* args, tasft_stream_t stream);
 
 /* Threshold given fp32 scores: hard = (soft >= tau) (& block tril when causal),

@@ -117,7 +117,7 @@ class GateBwdArgs(C.Structure):
 
 # name -> (argtypes, restype); every symbol declared in include/tasft_b200.h
 SIGNATURES = {
-    "tasft_gate_workspace_size": ([C.c_int32] * 7, C.c_int64),
+    "tasft_gate_workspace_size": ([C.c_int32] * 8, C.c_int64),
     "tasft_gate_mask_build": ([C.POINTER(GateArgs), vp], C.c_int),
     "tasft_mask_from_scores": ([C.POINTER(ThresholdArgs), vp], C.c_int),
     "tasft_mask_to_kept": ([C.POINTER(MaskArgs), vp], C.c_int),

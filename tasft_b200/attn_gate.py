@@ -158,7 +158,7 @@ class AttnGate(nn.Module):
         pq = torch.empty(B, Hq, nbq, D, dtype=torch.float32, device=dev) if want_pooled else None
         pk = torch.empty(B, Hk, nbk, D, dtype=torch.float32, device=dev) if want_pooled else None
         lib = L.lib()
-        ws_bytes = lib.tasft_gate_workspace_size(B, Hq, Hk, Sq, Sk, blk, hid)
+        ws_bytes = lib.tasft_gate_workspace_size(B, Hq, Hk, Sq, Sk, blk, hid, D)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         args = L.GateArgs(
             q=q.data_ptr(), k=k.data_ptr(), q_stride=L.strides4(q), k_stride=L.strides4(k),

@@ -109,6 +109,142 @@ __global__ void __launch_bounds__(kPoolThreads) gate_pool_project_kernel(tasft_g
 }
 
 // ---------------------------------------------------------------------------
+// Kernel 1 fast path, two passes.
+// 1a: one thread per (tensor, b, head, block, 16-byte column vector) sums that column over
+//     the block's rows by itself: no cross-thread reduction, few registers, many loads in
+//     flight; a warp reads two rows' 256 contiguous bytes per step. The fp32 means go to
+//     the caller's pooled outputs when given, else to the workspace.
+// 1b: the projection of 64 pooled rows per CTA through one half of W_in, as a small
+//     matrix product out of shared memory: W transposed (hidden fastest), the 64 means
+//     row-major; thread (row octet, hidden unit) accumulates 8 outputs, reading its weight
+//     once per d and the means as warp-wide broadcasts.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void add_bf16x8(const uint4& u, uint64_t (&acc)[4]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // bf16 -> fp32 is the 16-bit pattern in the high half of the word
+    const uint64_t pair = ((uint64_t)(w[i] & 0xffff0000u) << 32) | (uint64_t)(w[i] << 16);
+    asm("add.f32x2 %0, %0, %1;" : "+l"(acc[i]) : "l"(pair));
+  }
+}
+
+template <typename T, int EPV>
+__global__ void __launch_bounds__(kPoolThreads) gate_pool_kernel(tasft_gate_args a, float* mq, float* mk, int NBq,
+                                                                int NBk, int lcv) {
+  const int CV = 1 << lcv;
+  const int D = a.D;
+  int t = blockIdx.x * kPoolThreads + threadIdx.x;
+  const int nq = a.B * a.Hq * NBq * CV;
+  const int nk = a.B * a.Hk * NBk * CV;
+  if (t >= nq + nk) return;
+  const bool isq = t < nq;
+  if (!isq) t -= nq;
+  const int c = t & (CV - 1);
+  const int row = t >> lcv;  // (b * H + h) * NB + blk
+  const int H = isq ? a.Hq : a.Hk, NB = isq ? NBq : NBk, S = isq ? a.Sq : a.Sk;
+  const int blk = row % NB, bh = row / NB;
+  const int h = bh % H, b = bh / H;
+  const int64_t* st = isq ? a.q_stride : a.k_stride;
+  const T* p = reinterpret_cast<const T*>(isq ? a.q : a.k) + b * st[0] + h * st[1] +
+               (int64_t)blk * a.block * st[2] + c * EPV;
+  const int rows = min(a.block, S - blk * a.block);  // padding rows count as zeros
+  const int64_t rs = st[2];
+  float f[EPV];
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) add_bf16x8(__ldg(reinterpret_cast<const uint4*>(p + r * rs)), acc);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float((uint32_t)acc[i]);
+      f[2 * i + 1] = __uint_as_float((uint32_t)(acc[i] >> 32));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) f[e] = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) {
+      float g[EPV];
+      Vec16<T>::unpack(__ldg(reinterpret_cast<const uint4*>(p + r * rs)), g);
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) f[e] += g[e];
+    }
+  }
+  const float inv = 1.0f / (float)a.block;
+  float* out = (isq ? mq : mk) + (int64_t)row * D + c * EPV;
+#pragma unroll
+  for (int e = 0; e < EPV; e += 4)
+    *reinterpret_cast<float4*>(out + e) = make_float4(f[e] * inv, f[e + 1] * inv, f[e + 2] * inv, f[e + 3] * inv);
+}
+
+
+template <int HID>
+__global__ void __launch_bounds__(kPoolThreads) gate_project_kernel(tasft_gate_args a, const float* mq,
+                                                                   const float* mk, float* A, float* Ct, int NBq,
+                                                                   int NBk) {
+  extern __shared__ __align__(16) float psm[];  // w [HID][D + 1] (padded), then means [RPC][D]
+  constexpr int RPC = kPoolThreads / HID;      // rows per CTA: one (row, hidden unit) per thread
+  const int D = a.D;
+  const int rq = a.B * a.Hq * NBq, rk = a.B * a.Hk * NBk;
+  const int tq = (rq + RPC - 1) / RPC;
+  const bool isq = (int)blockIdx.x < tq;
+  const int r0 = (isq ? blockIdx.x : blockIdx.x - tq) * RPC;
+  const int nrows = min(RPC, (isq ? rq : rk) - r0);
+  const int DP = D + 1;  // row pitch: lanes (units j) reading one d hit distinct banks
+  float* wt = psm;
+  float* ms = psm + ((HID * DP + 3) & ~3);
+  const int off = isq ? 0 : D;
+  // 16-byte reads, unrolled so a thread's loads are in flight together (a rolled loop
+  // waits one L2 round trip per element before the compute can start)
+#pragma unroll 8
+  for (int x = threadIdx.x; x < HID * D / 4; x += kPoolThreads) {
+    const int j = x / (D / 4), d = (x % (D / 4)) * 4;
+    const float4 v = __ldg(reinterpret_cast<const float4*>(a.w_in + (int64_t)j * 2 * D + off + d));
+    float* w = wt + j * DP + d;
+    w[0] = v.x;
+    w[1] = v.y;
+    w[2] = v.z;
+    w[3] = v.w;
+  }
+  const float4* src = reinterpret_cast<const float4*>((isq ? mq : mk) + (int64_t)r0 * D);
+  for (int x = threadIdx.x; x < nrows * D / 4; x += kPoolThreads) reinterpret_cast<float4*>(ms)[x] = src[x];
+  __syncthreads();
+  const int j = threadIdx.x % HID, r = threadIdx.x / HID;
+  if (r >= nrows) return;
+  const float* m = ms + r * D;
+  const float* w = wt + j * DP;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (int d = 0; d < D; d += 4) {
+    const float4 mv = *reinterpret_cast<const float4*>(m + d);  // broadcast within the warp
+    s0 = fmaf(mv.x, w[d], s0);
+    s1 = fmaf(mv.y, w[d + 1], s1);
+    s2 = fmaf(mv.z, w[d + 2], s2);
+    s3 = fmaf(mv.w, w[d + 3], s3);
+  }
+  const float sv = (s0 + s1) + (s2 + s3);
+  const int rr = r0 + r;
+  if (isq) {
+    A[(int64_t)rr * HID + j] = sv + a.b_in[j];
+  } else {
+    const int blk = rr % NBk, bh = rr / NBk;
+    Ct[((int64_t)bh * HID + j) * NBk + blk] = sv;
+  }
+}
+
+template <int HID>
+static void launch_project(const tasft_gate_args& a, const float* mq, const float* mk, float* A, float* Ct, int NBq,
+                           int NBk, cudaStream_t st) {
+  constexpr int RPC = kPoolThreads / HID;
+  const int rq = a.B * a.Hq * NBq, rk = a.B * a.Hk * NBk;
+  const int grid = ceil_div(rq, RPC) + ceil_div(rk, RPC);
+  const size_t smem = (size_t)(((HID * (a.D + 1) + 3) & ~3) + RPC * a.D) * sizeof(float);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(gate_project_kernel<HID>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  gate_project_kernel<HID><<<grid, kPoolThreads, smem, st>>>(a, mq, mk, A, Ct, NBq, NBk);
+}
+
+// ---------------------------------------------------------------------------
 // Kernel 2: one warp per (b, q-head, q-block) row of the score grid.
 //   soft[j] = sigmoid(w_out . relu(a_i + c_j)), zeroed for j > i when causal and NBq == NBk
 //   hard[j] = soft[j] >= tau                                        (attn_gate.py:475)
@@ -177,6 +313,80 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_kernel(tasft_gate_
   }
 }
 
+// The same row computation with the kv-head's projected K rows (Ct slab, hid x NBk)
+// staged in shared memory once per CTA: a CTA takes 8 q-rows of one (b, kv-head) (the
+// group's q-heads read the same slab), one warp per row, lanes over k-blocks.
+constexpr int kSlabRows = 8;  // one row per warp: many CTAs for latency hiding
+
+__global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_slab_kernel(tasft_gate_args a, const float* A,
+                                                                          const float* Ct, int NBq, int NBk) {
+  extern __shared__ float sm[];  // ct [hid][NBk], arows [kSlabRows][hid], wout [hid]
+  const int hid = a.hidden;
+  const int grp = a.Hq / a.Hk;
+  const int per_bk = grp * NBq;  // q-rows of one (b, kv-head)
+  const int chunks = (per_bk + kSlabRows - 1) / kSlabRows;
+  const int bk = blockIdx.x / chunks;  // b * Hk + hk
+  const int lr0 = (blockIdx.x % chunks) * kSlabRows;
+  const int nrows = min(kSlabRows, per_bk - lr0);
+  const int b = bk / a.Hk, hk = bk % a.Hk;
+  float* ct = sm;
+  float* arows = sm + hid * NBk;
+  float* wout = arows + kSlabRows * hid;
+  const float* src = Ct + (int64_t)bk * hid * NBk;
+#pragma unroll 8
+  for (int x = threadIdx.x; x < hid * NBk; x += blockDim.x) ct[x] = __ldg(src + x);
+  for (int x = threadIdx.x; x < nrows * hid; x += blockDim.x) {
+    const int r = x / hid, lr = lr0 + r;
+    const int64_t row = ((int64_t)b * a.Hq + hk * grp + lr / NBq) * NBq + lr % NBq;
+    arows[x] = A[row * hid + x % hid];
+  }
+  for (int j = threadIdx.x; j < hid; j += blockDim.x) wout[j] = a.w_out[j];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool causal = a.causal && (NBq == NBk);
+  // kept blocks of the whole CTA, added to the global counter once (a counter hit by every
+  // row serialises at one L2 slice)
+  __shared__ int cta_kept;
+  if (threadIdx.x == 0) cta_kept = 0;
+  __syncthreads();
+  int warp_kept = 0;
+  for (int r = warp; r < nrows; r += kRowsPerCta) {
+    const int lr = lr0 + r;
+    const int i = lr % NBq;
+    const int64_t row = ((int64_t)b * a.Hq + hk * grp + lr / NBq) * NBq + i;
+    const float* ar = arows + r * hid;
+    int cnt = 0, kept_total = 0;
+    for (int j0 = 0; j0 < NBk; j0 += 32) {
+      const int j = j0 + lane;
+      const bool in_range = j < NBk;
+      float s = 0.f;
+      if (in_range) {
+        float l0 = 0.f, l1 = 0.f;
+        int h = 0;
+        for (; h + 1 < hid; h += 2) {
+          l0 = fmaf(wout[h], fmaxf(ar[h] + ct[h * NBk + j], 0.f), l0);
+          l1 = fmaf(wout[h + 1], fmaxf(ar[h + 1] + ct[(h + 1) * NBk + j], 0.f), l1);
+        }
+        if (h < hid) l0 = fmaf(wout[h], fmaxf(ar[h] + ct[h * NBk + j], 0.f), l0);
+        s = 1.0f / (1.0f + __expf(-(l0 + l1)));
+        if (causal && j > i) s = 0.f;
+        a.soft[row * NBk + j] = s;
+      }
+      const bool keep = in_range && (s >= a.tau);
+      kept_total += __popc(__ballot_sync(0xffffffffu, keep));
+      emit_row(s, j, NBk, in_range, !(causal && j > i), a.tau, row, a.hard, a.kept_idx, cnt);
+    }
+    if (a.kept_idx) {
+      for (int j = cnt + lane; j < NBk; j += 32) a.kept_idx[row * NBk + j] = -1;
+    }
+    if (lane == 0 && a.kept_cnt) a.kept_cnt[row] = cnt;
+    warp_kept += kept_total;
+  }
+  if (lane == 0 && warp_kept) atomicAdd(&cta_kept, warp_kept);
+  __syncthreads();
+  if (threadIdx.x == 0 && a.num_kept && cta_kept) atomicAdd(a.num_kept, cta_kept);
+}
+
 // ---------------------------------------------------------------------------
 // Threshold from given fp32 scores (bit-exact `soft >= tau`).
 // ---------------------------------------------------------------------------
@@ -229,21 +439,36 @@ __global__ void mask_to_kept_kernel(tasft_mask_args a) {
 using namespace tasft;
 
 extern "C" int64_t tasft_gate_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t Sq, int32_t Sk, int32_t block,
-                                             int32_t hidden) {
-  if (B <= 0 || Hq <= 0 || Hk <= 0 || Sq <= 0 || Sk <= 0 || block <= 0 || hidden <= 0) return -1;
+                                             int32_t hidden, int32_t D) {
+  if (B <= 0 || Hq <= 0 || Hk <= 0 || Sq <= 0 || Sk <= 0 || block <= 0 || hidden <= 0 || D <= 0) return -1;
   const int64_t NBq = ceil_div(Sq, block), NBk = ceil_div(Sk, block);
-  const int64_t floats = (int64_t)B * Hq * NBq * hidden + (int64_t)B * Hk * NBk * hidden;
+  const int64_t rows = (int64_t)B * Hq * NBq + (int64_t)B * Hk * NBk;
+  // [projected rows: A then Ct] [fp32 block means: Q rows then K rows, 256-byte aligned]
+  const int64_t floats = (rows * hidden + 63) / 64 * 64 + rows * D;
   return ((floats * 4 + 255) / 256) * 256;
 }
 
 template <typename T>
-static int launch_pool(const tasft_gate_args& a, float* A, float* Ct, int NBq, int NBk, cudaStream_t st) {
+static int launch_pool(const tasft_gate_args& a, float* A, float* Ct, float* mq, float* mk, int NBq, int NBk,
+                       cudaStream_t st) {
   constexpr int EPV = 16 / sizeof(T);
   const bool vec_ok = (a.D % EPV == 0) && aligned16(a.q) && aligned16(a.k) && (a.q_stride[0] % EPV == 0) &&
                       (a.q_stride[1] % EPV == 0) && (a.q_stride[2] % EPV == 0) && (a.k_stride[0] % EPV == 0) &&
                       (a.k_stride[1] % EPV == 0) && (a.k_stride[2] % EPV == 0) && (a.D / EPV <= kPoolThreads);
   const int64_t grid = (int64_t)a.B * a.Hq * NBq + (int64_t)a.B * a.Hk * NBk;
-  if (vec_ok) {
+  // fast path: hidden 32 or 64 (the gate's default is max(32, D/4)) and D <= 128, so the
+  // projection's shared memory (D * (hidden + 256 / hidden) floats) stays under 48 KB
+  const int CV = a.D / EPV;
+  const int64_t nthreads = ((int64_t)a.B * a.Hq * NBq + (int64_t)a.B * a.Hk * NBk) * CV;
+  if (vec_ok && (CV & (CV - 1)) == 0 && a.D % 4 == 0 && a.D <= 128 && (a.hidden == 32 || a.hidden == 64) &&
+      nthreads < (1LL << 31) - kPoolThreads && aligned16(mq) && aligned16(mk)) {
+    int lcv = 0;
+    while ((1 << lcv) < CV) ++lcv;
+    gate_pool_kernel<T, EPV><<<ceil_div(nthreads, kPoolThreads), kPoolThreads, 0, st>>>(a, mq, mk, NBq, NBk, lcv);
+    if (a.hidden == 32) launch_project<32>(a, mq, mk, A, Ct, NBq, NBk, st);
+    else launch_project<64>(a, mq, mk, A, Ct, NBq, NBk, st);
+    count_launch();
+  } else if (vec_ok) {
     const int RG = kPoolThreads / (a.D / EPV);
     const size_t smem = (size_t)(RG + 1) * a.D * sizeof(float);
     gate_pool_project_kernel<T, EPV><<<(unsigned)grid, kPoolThreads, smem, st>>>(a, A, Ct, NBq, NBk);
@@ -268,23 +493,37 @@ extern "C" int tasft_gate_mask_build(const tasft_gate_args* ap, tasft_stream_t s
   if (a.D > 1024) return TASFT_ERR_UNSUPPORTED;
   if ((a.kept_idx == nullptr) != (a.kept_cnt == nullptr)) return TASFT_ERR_INVALID_ARG;
   if (a.q_stride[3] != 1 || a.k_stride[3] != 1) return TASFT_ERR_INVALID_ARG;
-  const int64_t need = tasft_gate_workspace_size(a.B, a.Hq, a.Hk, a.Sq, a.Sk, a.block, a.hidden);
+  const int64_t need = tasft_gate_workspace_size(a.B, a.Hq, a.Hk, a.Sq, a.Sk, a.block, a.hidden, a.D);
   if (!a.workspace || a.workspace_bytes < need) return TASFT_ERR_WORKSPACE;
   const int NBq = ceil_div(a.Sq, a.block), NBk = ceil_div(a.Sk, a.block);
   float* A = reinterpret_cast<float*>(a.workspace);
   float* Ct = A + (int64_t)a.B * a.Hq * NBq * a.hidden;
+  // block means: the caller's pooled outputs when given, else the workspace's tail
+  float* means = A + ((int64_t)a.B * a.Hq * NBq * a.hidden + (int64_t)a.B * a.Hk * NBk * a.hidden + 63) / 64 * 64;
+  float* mq = a.pooled_q ? a.pooled_q : means;
+  float* mk = a.pooled_k ? a.pooled_k : means + (int64_t)a.B * a.Hq * NBq * a.D;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int rc;
   switch (a.dtype) {
-    case TASFT_F32: rc = launch_pool<float>(a, A, Ct, NBq, NBk, st); break;
-    case TASFT_BF16: rc = launch_pool<__nv_bfloat16>(a, A, Ct, NBq, NBk, st); break;
-    case TASFT_F16: rc = launch_pool<__half>(a, A, Ct, NBq, NBk, st); break;
+    case TASFT_F32: rc = launch_pool<float>(a, A, Ct, mq, mk, NBq, NBk, st); break;
+    case TASFT_BF16: rc = launch_pool<__nv_bfloat16>(a, A, Ct, mq, mk, NBq, NBk, st); break;
+    case TASFT_F16: rc = launch_pool<__half>(a, A, Ct, mq, mk, NBq, NBk, st); break;
     default: return TASFT_ERR_UNSUPPORTED;
   }
   if (rc != TASFT_OK) return rc;
-  const int64_t rows = (int64_t)a.B * a.Hq * NBq;
-  const size_t smem = (size_t)(kRowsPerCta + 1) * a.hidden * sizeof(float);
-  gate_pair_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, smem, st>>>(a, A, Ct, NBq, NBk);
+  const size_t slab = (size_t)(a.hidden * NBk + kSlabRows * a.hidden + a.hidden) * sizeof(float);
+  if (slab <= 96 * 1024) {
+    auto kern = gate_pair_slab_kernel;
+    if (slab > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slab) != cudaSuccess)
+      return TASFT_ERR_CUDA;
+    const int64_t grid = (int64_t)a.B * a.Hk * ceil_div((int64_t)(a.Hq / a.Hk) * NBq, kSlabRows);
+    kern<<<(unsigned)grid, kRowsPerCta * 32, slab, st>>>(a, A, Ct, NBq, NBk);
+  } else {
+    const int64_t rows = (int64_t)a.B * a.Hq * NBq;
+    const size_t smem = (size_t)(kRowsPerCta + 1) * a.hidden * sizeof(float);
+    gate_pair_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, smem, st>>>(a, A, Ct, NBq, NBk);
+  }
   count_launch();
   return launch_status();
 }

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = L.lib()
-    assert lib.tasft_abi_version() == 1
+    assert lib.tasft_abi_version() == 2
     assert lib.tasft_status_string(0) == b"ok"
     assert b"argument" in lib.tasft_status_string(-1)
     assert lib.tasft_launch_count() >= 0
@@ -66,8 +66,9 @@ def test_prefill_bad_shapes_rejected():
 
 def test_workspace_sizes():
     lib = L.lib()
-    assert lib.tasft_gate_workspace_size(4, 32, 8, 4096, 4096, 64, 32) == (4 * 32 * 64 * 32 + 4 * 8 * 64 * 32) * 4
-    assert lib.tasft_gate_workspace_size(0, 1, 1, 1, 1, 1, 1) == -1
+    rows = 4 * 32 * 64 + 4 * 8 * 64
+    assert lib.tasft_gate_workspace_size(4, 32, 8, 4096, 4096, 64, 32, 128) == rows * 32 * 4 + rows * 128 * 4
+    assert lib.tasft_gate_workspace_size(0, 1, 1, 1, 1, 1, 1, 64) == -1
     assert lib.tasft_decode_workspace_size(64, 32, 8, 128, 4) >= 64 * 32 * 4 * 130 * 4
     assert lib.tasft_gate_target_workspace_size(4, 32, 4096, 64) == 4 * 32 * 64 * 64 * 4
     assert lib.tasft_gate_loss_workspace_size(4, 32) > 0
