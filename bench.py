@@ -386,12 +386,37 @@ def run_ours(args):
         o = kern.forward(qd, kd, vd, md)
         oh.copy_(o, non_blocking=True)
 
+    # the same calls pipelined over the batch on two streams: H2D of sequence b + 1, the
+    # kernels of b and D2H of b - 1 overlap (copy engines run both directions at once)
+    main = torch.cuda.current_stream()
+    lanes = [torch.cuda.Stream() for _ in range(2)]
+    slots = [(torch.empty_like(q[:1]), torch.empty_like(k[:1]), torch.empty_like(v[:1]),
+              torch.empty_like(mask[:1])) for _ in range(2)]
+
+    def step_e2e_pipe():
+        for s_ in lanes:
+            s_.wait_stream(main)
+        for bi in range(qh.shape[0]):
+            s_ = lanes[bi % 2]
+            qd, kd, vd, md = slots[bi % 2]
+            with torch.cuda.stream(s_):
+                qd.copy_(qh[bi:bi + 1], non_blocking=True)
+                kd.copy_(kh[bi:bi + 1], non_blocking=True)
+                vd.copy_(vh[bi:bi + 1], non_blocking=True)
+                md.copy_(mh[bi:bi + 1], non_blocking=True)
+                o = kern.forward(qd, kd, vd, md)
+                oh[bi:bi + 1].copy_(o, non_blocking=True)
+        for s_ in lanes:
+            main.wait_stream(s_)
+
     e2e_steps = max(3, min(args.steps, 10))
-    t_e2e = time_steps(step_e2e, e2e_steps, max(args.warmup, 3), flush, ws)
+    t_e2e_serial = time_steps(step_e2e, e2e_steps, max(args.warmup, 3), flush, ws)
+    ms_e2e_serial = max_over_ranks(statistics.mean(t_e2e_serial), ws)
+    t_e2e = time_steps(step_e2e_pipe, e2e_steps, max(args.warmup, 3), flush, ws)
     ms_e2e = max_over_ranks(statistics.mean(t_e2e), ws)
     h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2 + mh.numel()
     d2h = oh.numel() * 2
-    del qh, kh, vh, oh, mh, q, k, v, out, kept
+    del qh, kh, vh, oh, mh, q, k, v, out, kept, slots
 
     # ---------------- decode ----------------
     qd, kc, vc, kv_len, dkept = make_decode_inputs(1234 + 3 + 1000 * rank, dev)
@@ -467,7 +492,9 @@ def run_ours(args):
             "roofline": roofline,
             "e2e": {"value": round(total_flops / (ms_e2e * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 3),
-                    "api": "tasft_b200.BlockSparseFlashAttention.forward(q, k, v, bool mask) from pinned host"},
+                    "api": "tasft_b200.BlockSparseFlashAttention.forward(q, k, v, bool mask) from pinned host, "
+                           "one call per sequence, copies and calls pipelined on two streams",
+                    "ms_per_step_unpipelined": round(ms_e2e_serial, 3)},
             "decode": decode,
             "gate": gate_info,
             "gate_target": target_info,
