@@ -190,6 +190,26 @@ TASFT_API int tasft_bsa_decode_fwd(const tasft_decode_args* args, tasft_stream_t
 TASFT_API int tasft_bsa_decode_fwd_noalloc(const tasft_decode_args* args, tasft_stream_t stream);
 TASFT_API int64_t tasft_decode_noalloc_capacity(void);
 
+/* Block-sparse decode over a PAGED KV cache (vLLM's flash layout). No counterpart in the
+ * reference: its vLLM backend runs decode dense over paged caches
+ * (tasft/inference/vllm_patch.py:189-196); this is the sparse replacement for that call.
+ * `base` is read as for tasft_bsa_decode_fwd except:
+ *   base.k_cache / base.v_cache  page pools [num_pages, page_size, Hk, D]
+ *   base.k_stride / base.v_stride element strides of those pools (stride[3] == 1)
+ *   base.L                       logical capacity = max_pages * page_size
+ * Logical token t of sequence b lives in page block_table[b * max_pages + t / page_size]
+ * at row t % page_size. Kept lists stay in logical 64-token blocks. bf16/fp16, D 64 or
+ * 128, block 64, page_size 16, 32, 64 or 128. A table entry outside [0, num_pages) is
+ * skipped and reported as TASFT_DEVERR_INDEX. */
+typedef struct {
+  tasft_decode_args base;
+  const int32_t* block_table; /* [B, max_pages] */
+  int32_t max_pages;
+  int32_t page_size;
+  int32_t num_pages;
+} tasft_paged_decode_args;
+TASFT_API int tasft_bsa_decode_paged_fwd(const tasft_paged_decode_args* args, tasft_stream_t stream);
+
 /* Merge G partial results (normalised o, m, l) into the final output. */
 typedef struct {
   const float* part_o;    /* [G, rows, D] fp32 */

@@ -14,7 +14,7 @@ from tasft_b200.block_sparse_fa import (
     detect_kernels,
     mask_to_kept,
 )
-from tasft_b200.decode import DecodeWorkspace, bsa_decode, decode_combine
+from tasft_b200.decode import DecodeWorkspace, bsa_decode, bsa_decode_paged, decode_combine
 from tasft_b200.exceptions import KernelError, NaNDetectedError, TASFTError, ValidationError
 from tasft_b200.patch import patch, unpatch
 from tasft_b200 import shards
@@ -36,6 +36,7 @@ __all__ = [
     "TASFTObjective",
     "ValidationError",
     "bsa_decode",
+    "bsa_decode_paged",
     "decode_combine",
     "detect_kernels",
     "gate_losses",

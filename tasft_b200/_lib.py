@@ -79,6 +79,13 @@ class DecodeArgs(C.Structure):
     ]
 
 
+class PagedDecodeArgs(C.Structure):
+    _fields_ = [
+        ("base", DecodeArgs), ("block_table", vp), ("max_pages", C.c_int32), ("page_size", C.c_int32),
+        ("num_pages", C.c_int32),
+    ]
+
+
 class CombineArgs(C.Structure):
     _fields_ = [
         ("part_o", vp), ("part_ml", vp), ("G", C.c_int32), ("rows", C.c_int64), ("D", C.c_int32),
@@ -126,6 +133,7 @@ SIGNATURES = {
     "tasft_bsa_decode_fwd": ([C.POINTER(DecodeArgs), vp], C.c_int),
     "tasft_bsa_decode_combine": ([C.POINTER(CombineArgs), vp], C.c_int),
     "tasft_bsa_decode_fwd_noalloc": ([C.POINTER(DecodeArgs), vp], C.c_int),
+    "tasft_bsa_decode_paged_fwd": ([C.POINTER(PagedDecodeArgs), vp], C.c_int),
     "tasft_decode_noalloc_capacity": ([], C.c_int64),
     "tasft_gate_target_workspace_size": ([C.c_int32] * 4, C.c_int64),
     "tasft_gate_target_fwd": ([C.POINTER(TargetArgs), vp], C.c_int),

@@ -450,3 +450,35 @@ int decode_run(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaS
 }
 
 }  // namespace tasft
+
+using namespace tasft;
+
+// Paged KV cache: the same tensor-core decode, with K/V loaded through the block table.
+extern "C" int tasft_bsa_decode_paged_fwd(const tasft_paged_decode_args* pp, tasft_stream_t stream) {
+  if (!pp) return TASFT_ERR_INVALID_ARG;
+  const tasft_decode_args& a = pp->base;
+  if (!a.q || !a.k_cache || !a.v_cache || !a.kv_len || !a.kept_idx || !a.kept_cnt || !pp->block_table)
+    return TASFT_ERR_INVALID_ARG;
+  if (!a.out && !a.part_o) return TASFT_ERR_INVALID_ARG;
+  if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.D <= 0 || a.block <= 0 || a.nb_max <= 0 || a.Hq % a.Hk)
+    return TASFT_ERR_INVALID_ARG;
+  const int ps = pp->page_size;
+  if (ps != 16 && ps != 32 && ps != 64 && ps != 128) return TASFT_ERR_UNSUPPORTED;
+  if (pp->max_pages <= 0 || pp->num_pages <= 0 || (int64_t)pp->max_pages * ps != a.L) return TASFT_ERR_INVALID_ARG;
+  if (a.dtype != TASFT_BF16 && a.dtype != TASFT_F16) return TASFT_ERR_UNSUPPORTED;
+  // page pools [num_pages, page_size, Hk, D], D contiguous; TMA wants 16-byte strides and base
+  if (a.k_stride[3] != 1 || a.v_stride[3] != 1 || a.q_stride[2] != 1 || (a.out && a.o_stride[2] != 1))
+    return TASFT_ERR_INVALID_ARG;
+  for (int i = 0; i < 3; ++i)
+    if ((a.k_stride[i] * 2) % 16 || (a.v_stride[i] * 2) % 16) return TASFT_ERR_INVALID_ARG;
+  if (!aligned16(a.k_cache) || !aligned16(a.v_cache)) return TASFT_ERR_INVALID_ARG;
+  const int nsplit = decode_pick_splits(a);
+  DecodeWs ws{nullptr, nullptr, 0};
+  if (nsplit > 1) {
+    if (!a.workspace) return TASFT_ERR_WORKSPACE;
+    const int rc = decode_ws_from(a, nsplit, &ws);
+    if (rc != TASFT_OK) return rc;
+  }
+  return decode_mma_paged(a, ws, nsplit, pp->block_table, pp->max_pages, ps, pp->num_pages,
+                          reinterpret_cast<cudaStream_t>(stream));
+}

@@ -83,5 +83,8 @@ __device__ void decode_finish(const tasft_decode_args& a, const DecodeWs& ws, in
 }
 
 int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st);
+// Paged-cache variant (k_cache / v_cache are page pools, see tasft_bsa_decode_paged_fwd).
+int decode_mma_paged(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const int32_t* table, int max_pages,
+                     int page_size, int num_pages, cudaStream_t st);
 
 }  // namespace tasft

@@ -105,16 +105,22 @@ __device__ __forceinline__ int next_item(int32_t* ctr, int& k, int items) {
   return it < items ? it : -1;
 }
 
+// Page-pool geometry of a paged cache (unused by the contiguous kernel).
+struct PagedInfo {
+  const int32_t* table;  // [B, max_pages] physical page of each logical page
+  int max_pages, page_size, num_pages;
+};
+
 __device__ __forceinline__ uint32_t movm_t(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
 
-template <int D, bool kF16>
+template <int D, bool kF16, bool kPaged>
 __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
     bsa_decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                          const tasft_decode_args a, const DecodeWs ws, const int nsplit) {
+                          const tasft_decode_args a, const DecodeWs ws, const int nsplit, const PagedInfo pg) {
   using T = typename std::conditional<kF16, __half, __nv_bfloat16>::type;
   constexpr int kTile = (D / 64) * kSub * 128;  // bytes of one K (or V) half-block tile
   constexpr int kStage = 2 * kTile;
@@ -156,17 +162,51 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
           set_err(a.err, TASFT_DEVERR_TIMEOUT);
           return false;
         }
-        tags[s] = t;
-        if (t.item >= 0 && t.n > 0 && t.kb >= 0 && t.kb < NBk) {
-          const int unit = t.item / nsplit;
-          const int b = unit / a.Hk, hk = unit % a.Hk;
-          const int row = t.kb * kBlkM + (t.j & 1) * kSub;
+        Tag tt = t;
+        bool load = t.item >= 0 && t.n > 0 && t.kb >= 0 && t.kb < NBk;
+        const int unit = t.item >= 0 ? t.item / nsplit : 0;
+        const int b = unit / a.Hk, hk = unit % a.Hk;
+        const int row = t.kb * kBlkM + (t.j & 1) * kSub;  // logical token of the stage's first key
+        int pages[2] = {0, 0};                            // physical page(s) of the stage (paged)
+        if constexpr (kPaged) {
+          if (load) {
+            // a 32-key stage spans one page (page_size >= 32) or two 16-token pages
+            const int np = pg.page_size >= kSub ? 1 : kSub / pg.page_size;
+            for (int i = 0; i < np; ++i) {
+              const int lp = (row + i * pg.page_size) / pg.page_size;
+              const int ph = lp < pg.max_pages ? pg.table[(int64_t)b * pg.max_pages + lp] : -1;
+              if (ph < 0 || ph >= pg.num_pages) load = false;
+              pages[i] = ph;
+            }
+            if (!load) {
+              set_err(a.err, TASFT_DEVERR_INDEX);
+              tt.kb = -1;  // the consumer skips the stage
+            }
+          }
+        }
+        tags[s] = tt;
+        if (load) {
           uint8_t* sk = smem + s * kStage;
           mbar_arrive_expect_tx(&full[s], kStage);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c) {
-            tc::tma_load_4d(sk + c * kSub * 128, &tmk, c * 64, row, hk, b, &full[s]);
-            tc::tma_load_4d(sk + kTile + c * kSub * 128, &tmv, c * 64, row, hk, b, &full[s]);
+            if constexpr (kPaged) {
+              if (pg.page_size >= kSub) {
+                const int off = row % pg.page_size;
+                tc::tma_load_4d(sk + c * kSub * 128, &tmk, c * 64, hk, off, pages[0], &full[s]);
+                tc::tma_load_4d(sk + kTile + c * kSub * 128, &tmv, c * 64, hk, off, pages[0], &full[s]);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  tc::tma_load_4d(sk + c * kSub * 128 + i * 16 * 128, &tmk, c * 64, hk, 0, pages[i], &full[s]);
+                  tc::tma_load_4d(sk + kTile + c * kSub * 128 + i * 16 * 128, &tmv, c * 64, hk, 0, pages[i],
+                                  &full[s]);
+                }
+              }
+            } else {
+              tc::tma_load_4d(sk + c * kSub * 128, &tmk, c * 64, row, hk, b, &full[s]);
+              tc::tma_load_4d(sk + kTile + c * kSub * 128, &tmv, c * 64, row, hk, b, &full[s]);
+            }
           }
         } else {
           mbar_arrive(&full[s]);
@@ -435,17 +475,25 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
   __syncwarp();
 }
 
-template <int D, bool kF16>
-int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st) {
+template <int D, bool kF16, bool kPaged>
+int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const PagedInfo& pg, cudaStream_t st) {
   CUtensorMap mk, mv;
-  if (!make_tmap_bhsd(&mk, a.k_cache, a.B, a.Hk, a.L, D, a.k_stride, 2, kSub) ||
-      !make_tmap_bhsd(&mv, a.v_cache, a.B, a.Hk, a.L, D, a.v_stride, 2, kSub)) {
-    if (debug_enabled()) debug_log("decode: tensor map rejected, using the CUDA-core kernel");
+  bool maps;
+  if constexpr (kPaged) {
+    const int rows = pg.page_size >= kSub ? kSub : pg.page_size;
+    maps = make_tmap_paged(&mk, a.k_cache, pg.num_pages, pg.page_size, a.Hk, D, a.k_stride, rows) &&
+           make_tmap_paged(&mv, a.v_cache, pg.num_pages, pg.page_size, a.Hk, D, a.v_stride, rows);
+  } else {
+    maps = make_tmap_bhsd(&mk, a.k_cache, a.B, a.Hk, a.L, D, a.k_stride, 2, kSub) &&
+           make_tmap_bhsd(&mv, a.v_cache, a.B, a.Hk, a.L, D, a.v_stride, 2, kSub);
+  }
+  if (!maps) {
+    if (debug_enabled()) debug_log("decode: tensor map rejected");
     return TASFT_ERR_UNSUPPORTED;
   }
   constexpr int kStage = 2 * (D / 64) * kSub * 128;
   const int smem = 1024 + kStages * kStage + 2 * kStages * 8 + kStages * (int)sizeof(Tag);
-  auto kern = bsa_decode_mma_kernel<D, kF16>;
+  auto kern = bsa_decode_mma_kernel<D, kF16, kPaged>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return TASFT_ERR_CUDA;
   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -457,23 +505,41 @@ int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaS
   const int64_t items = (int64_t)a.B * a.Hk * nsplit;
   int64_t grid = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
   if (grid > items) grid = items;
-  if (debug_enabled()) debug_log("decode_mma D=%d f16=%d grid=%lld smem=%d splits=%d", D, (int)kF16, (long long)grid, smem, nsplit);
-  kern<<<(unsigned)grid, kThreadsM, smem, st>>>(mk, mv, a, ws, nsplit);
+  if (debug_enabled())
+    debug_log("decode_mma D=%d f16=%d paged=%d grid=%lld smem=%d splits=%d", D, (int)kF16, (int)kPaged,
+              (long long)grid, smem, nsplit);
+  kern<<<(unsigned)grid, kThreadsM, smem, st>>>(mk, mv, a, ws, nsplit, pg);
   count_launch();
   return launch_status();
+}
+
+bool mma_ok(const tasft_decode_args& a) {
+  if (a.dtype != TASFT_BF16 && a.dtype != TASFT_F16) return false;
+  if (a.block != kBlkM || (a.D != 64 && a.D != 128)) return false;
+  if (a.Hq / a.Hk > 8) return false;  // q-heads of a group fill the MMA's N = 8
+  // Q fragments are read as aligned 32-bit pairs
+  if ((reinterpret_cast<uintptr_t>(a.q) & 3u) || (a.q_stride[0] & 1) || (a.q_stride[1] & 1)) return false;
+  return true;
+}
+
+template <bool kPaged>
+int dispatch(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const PagedInfo& pg, cudaStream_t st) {
+  if (!mma_ok(a)) return TASFT_ERR_UNSUPPORTED;
+  const bool f16 = a.dtype == TASFT_F16;
+  if (a.D == 128)
+    return f16 ? launch_mma<128, true, kPaged>(a, ws, nsplit, pg, st) : launch_mma<128, false, kPaged>(a, ws, nsplit, pg, st);
+  return f16 ? launch_mma<64, true, kPaged>(a, ws, nsplit, pg, st) : launch_mma<64, false, kPaged>(a, ws, nsplit, pg, st);
 }
 
 }  // namespace
 
 int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st) {
-  if (a.dtype != TASFT_BF16 && a.dtype != TASFT_F16) return TASFT_ERR_UNSUPPORTED;
-  if (a.block != kBlkM || (a.D != 64 && a.D != 128)) return TASFT_ERR_UNSUPPORTED;
-  if (a.Hq / a.Hk > 8) return TASFT_ERR_UNSUPPORTED;  // q-heads of a group fill the MMA's N = 8
-  // Q fragments are read as aligned 32-bit pairs
-  if ((reinterpret_cast<uintptr_t>(a.q) & 3u) || (a.q_stride[0] & 1) || (a.q_stride[1] & 1)) return TASFT_ERR_UNSUPPORTED;
-  const bool f16 = a.dtype == TASFT_F16;
-  if (a.D == 128) return f16 ? launch_mma<128, true>(a, ws, nsplit, st) : launch_mma<128, false>(a, ws, nsplit, st);
-  return f16 ? launch_mma<64, true>(a, ws, nsplit, st) : launch_mma<64, false>(a, ws, nsplit, st);
+  return dispatch<false>(a, ws, nsplit, PagedInfo{nullptr, 0, 0, 0}, st);
+}
+
+int decode_mma_paged(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const int32_t* table, int max_pages,
+                     int page_size, int num_pages, cudaStream_t st) {
+  return dispatch<true>(a, ws, nsplit, PagedInfo{table, max_pages, page_size, num_pages}, st);
 }
 
 }  // namespace tasft

@@ -161,6 +161,12 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
 // Host: build a 4-D bf16/f16 tensor map over [B, H, S, D] (innermost D) with a
 // (64 x 64) box and 128-byte swizzle. Returns false when strides/alignment do not
 // satisfy TMA rules (16-byte aligned base and strides).
+// Host: 4-D bf16/f16 map over a page pool [pages, page_size, H, D] (element strides
+// st[0..2], st[3] == 1) as dims {D, H, page_size, pages}; box {64, 1, box_rows, 1}, so a
+// box is box_rows tokens x 128 B of one head, 128-byte swizzled like make_tmap_bhsd's.
+bool make_tmap_paged(CUtensorMap* map, const void* base, int pages, int page_size, int H, int D,
+                     const int64_t* stride_elems, int box_rows);
+
 bool make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int S, int D, const int64_t* stride_elems,
                     int elem_bytes, int box_rows);
 

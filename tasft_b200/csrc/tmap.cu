@@ -42,4 +42,23 @@ bool make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int S, int
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_paged(CUtensorMap* map, const void* base, int pages, int page_size, int H, int D, const int64_t* st,
+                     int box_rows) {
+  auto fn = get_encode();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+  if (st[3] != 1 || D % 64 != 0) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((st[i] * 2) % 16 != 0 || st[i] <= 0) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)page_size, (cuuint64_t)pages};
+  cuuint64_t strides[3] = {(cuuint64_t)(st[2] * 2), (cuuint64_t)(st[1] * 2), (cuuint64_t)(st[0] * 2)};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS && debug_enabled()) debug_log("cuTensorMapEncodeTiled (paged) failed: %d", (int)r);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace tasft

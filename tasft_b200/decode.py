@@ -95,6 +95,69 @@ def bsa_decode(
     return out
 
 
+def bsa_decode_paged(
+    q: torch.Tensor,
+    k_pages: torch.Tensor,
+    v_pages: torch.Tensor,
+    block_table: torch.Tensor,
+    kv_len: torch.Tensor,
+    kept: KeptBlocks,
+    block: int = 64,
+    *,
+    num_splits: int = 0,
+    workspace: DecodeWorkspace | None = None,
+    out: torch.Tensor | None = None,
+    partials: tuple[torch.Tensor, torch.Tensor] | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor | None:
+    """Sparse decode over a paged KV cache (vLLM's flash layout).
+
+    ``k_pages`` / ``v_pages`` ``[num_pages, page_size, Hk, D]``; ``block_table``
+    ``[B, max_pages]`` int32 maps logical page ``t // page_size`` of sequence b to a
+    physical page; ``kept`` lists are in logical 64-token blocks, as for ``bsa_decode``.
+    The reference's vLLM backend decodes paged caches densely
+    (``tasft/inference/vllm_patch.py:189-196``); this is the sparse call for that site.
+    """
+    L.require_cuda(q, k_pages, v_pages, block_table, kv_len)
+    if q.ndim != 3 or k_pages.ndim != 4 or k_pages.shape != v_pages.shape or block_table.ndim != 2:
+        raise KernelError("paged decode expects q [B,Hq,D], pages [P,page,Hk,D], block_table [B,max_pages]",
+                          context={"q": list(q.shape), "k": list(k_pages.shape), "table": list(block_table.shape)})
+    B, Hq, D = q.shape
+    num_pages, page_size, Hk, _ = k_pages.shape
+    max_pages = block_table.shape[1]
+    if Hq % Hk or k_pages.shape[3] != D or block_table.shape[0] != B:
+        raise KernelError("paged decode shape mismatch", context={"q": list(q.shape), "k": list(k_pages.shape)})
+    q = q.contiguous()
+    table = block_table.to(torch.int32).contiguous()
+    idx = kept.idx.contiguous()
+    cnt = kept.cnt.contiguous()
+    if out is None and partials is None:
+        out = torch.empty_like(q)
+    ws_ptr, ws_bytes = None, 0
+    if num_splits != 1:
+        if workspace is None:
+            ms = num_splits if num_splits > 0 else 16
+            workspace = DecodeWorkspace(B, Hq, Hk, D, ms, q.device)
+        ws_ptr, ws_bytes = workspace.buf.data_ptr(), workspace.bytes
+        if num_splits <= 0:
+            num_splits = min(workspace.max_splits, default_splits(B, Hk, idx.shape[-1] / 4))
+    base = L.DecodeArgs(
+        q=q.data_ptr(), k_cache=k_pages.data_ptr(), v_cache=v_pages.data_ptr(), out=L.ptr(out),
+        q_stride=L.strides3(q), k_stride=L.strides4(k_pages), v_stride=L.strides4(v_pages),
+        o_stride=L.strides3(out) if out is not None else L.I64x3(0, 0, 0),
+        B=B, Hq=Hq, Hk=Hk, L=max_pages * page_size, D=D, block=block, dtype=L.dtype_code(q),
+        scale=1.0 / math.sqrt(D), kv_len=kv_len.data_ptr(), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(),
+        nb_max=idx.shape[-1], num_splits=num_splits, part_o=L.ptr(partials[0]) if partials else None,
+        part_ml=L.ptr(partials[1]) if partials else None, workspace=ws_ptr, workspace_bytes=ws_bytes,
+        err=L.ptr(err),
+    )
+    args = L.PagedDecodeArgs(base=base, block_table=table.data_ptr(), max_pages=max_pages, page_size=page_size,
+                             num_pages=num_pages)
+    L.check(L.lib().tasft_bsa_decode_paged_fwd(args, L.stream_ptr(q.device)), "tasft_bsa_decode_paged_fwd",
+            shape=[B, Hq, Hk, num_pages, page_size, D], splits=num_splits)
+    return out
+
+
 def decode_combine(part_o: torch.Tensor, part_ml: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
     """Merge G partials ``o [G,B,Hq,D]`` / ``ml [G,B,Hq,2]`` (e.g. all-gathered from G GPUs)."""
     L.require_cuda(part_o, part_ml)
@@ -110,4 +173,4 @@ def decode_combine(part_o: torch.Tensor, part_ml: torch.Tensor, out_dtype=torch.
     return out
 
 
-__all__ = ["DecodeWorkspace", "bsa_decode", "decode_combine", "default_splits"]
+__all__ = ["DecodeWorkspace", "bsa_decode", "bsa_decode_paged", "decode_combine", "default_splits"]
