@@ -130,7 +130,7 @@ __device__ __forceinline__ void add_bf16x8(const uint4& u, uint64_t (&acc)[4]) {
 }
 
 template <typename T, int EPV>
-__global__ void __launch_bounds__(kPoolThreads) gate_pool_kernel(tasft_gate_args a, float* mq, float* mk, int NBq,
+__global__ void __launch_bounds__(kPoolThreads, 6) gate_pool_kernel(tasft_gate_args a, float* mq, float* mk, int NBq,
                                                                 int NBk, int lcv) {
   const int CV = 1 << lcv;
   const int D = a.D;
