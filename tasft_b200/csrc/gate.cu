@@ -184,7 +184,8 @@ __global__ void __launch_bounds__(kPoolThreads) gate_project_kernel(tasft_gate_a
                                                                    const float* mk, float* A, float* Ct, int NBq,
                                                                    int NBk) {
   extern __shared__ __align__(16) float psm[];  // w [HID][D + 1] (padded), then means [RPC][D]
-  constexpr int RPC = kPoolThreads / HID;      // rows per CTA: one (row, hidden unit) per thread
+  constexpr int RPT = 4;                       // rows per thread: each weight read feeds 4 FMAs
+  constexpr int RPC = kPoolThreads / HID * RPT;  // rows per CTA
   const int D = a.D;
   const int rq = a.B * a.Hq * NBq, rk = a.B * a.Hk * NBk;
   const int tq = (rq + RPC - 1) / RPC;
@@ -210,32 +211,40 @@ __global__ void __launch_bounds__(kPoolThreads) gate_project_kernel(tasft_gate_a
   const float4* src = reinterpret_cast<const float4*>((isq ? mq : mk) + (int64_t)r0 * D);
   for (int x = threadIdx.x; x < nrows * D / 4; x += kPoolThreads) reinterpret_cast<float4*>(ms)[x] = src[x];
   __syncthreads();
-  const int j = threadIdx.x % HID, r = threadIdx.x / HID;
-  if (r >= nrows) return;
-  const float* m = ms + r * D;
+  const int j = threadIdx.x % HID, rg = threadIdx.x / HID;  // rows rg + i * (RPC / RPT)
+  constexpr int kStride = RPC / RPT;
+  if (rg >= nrows) return;
   const float* w = wt + j * DP;
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  float acc[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) acc[i] = 0.f;
   for (int d = 0; d < D; d += 4) {
-    const float4 mv = *reinterpret_cast<const float4*>(m + d);  // broadcast within the warp
-    s0 = fmaf(mv.x, w[d], s0);
-    s1 = fmaf(mv.y, w[d + 1], s1);
-    s2 = fmaf(mv.z, w[d + 2], s2);
-    s3 = fmaf(mv.w, w[d + 3], s3);
+    const float w0 = w[d], w1 = w[d + 1], w2 = w[d + 2], w3 = w[d + 3];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const int r = min(rg + i * kStride, nrows - 1);
+      const float4 mv = *reinterpret_cast<const float4*>(ms + r * D + d);  // broadcast within the warp
+      acc[i] = fmaf(mv.x, w0, fmaf(mv.y, w1, fmaf(mv.z, w2, fmaf(mv.w, w3, acc[i]))));
+    }
   }
-  const float sv = (s0 + s1) + (s2 + s3);
-  const int rr = r0 + r;
-  if (isq) {
-    A[(int64_t)rr * HID + j] = sv + a.b_in[j];
-  } else {
-    const int blk = rr % NBk, bh = rr / NBk;
-    Ct[((int64_t)bh * HID + j) * NBk + blk] = sv;
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int r = rg + i * kStride;
+    if (r >= nrows) break;
+    const int rr = r0 + r;
+    if (isq) {
+      A[(int64_t)rr * HID + j] = acc[i] + a.b_in[j];
+    } else {
+      const int blk = rr % NBk, bh = rr / NBk;
+      Ct[((int64_t)bh * HID + j) * NBk + blk] = acc[i];
+    }
   }
 }
 
 template <int HID>
 static void launch_project(const tasft_gate_args& a, const float* mq, const float* mk, float* A, float* Ct, int NBq,
                            int NBk, cudaStream_t st) {
-  constexpr int RPC = kPoolThreads / HID;
+  constexpr int RPC = kPoolThreads / HID * 4;
   const int rq = a.B * a.Hq * NBq, rk = a.B * a.Hk * NBk;
   const int grid = ceil_div(rq, RPC) + ceil_div(rk, RPC);
   const size_t smem = (size_t)(((HID * (a.D + 1) + 3) & ~3) + RPC * a.D) * sizeof(float);
