@@ -152,6 +152,24 @@ typedef struct {
 } tasft_prefill_args;
 TASFT_API int tasft_bsa_prefill_fwd(const tasft_prefill_args* args, tasft_stream_t stream);
 
+/* Prefill of a batch of sequences of different lengths packed along the token axis (the
+ * layout vLLM hands its attention backend). Replaces the reference's vLLM prefill, which
+ * flattens the batch into one causal sequence so sequences attend across their
+ * boundaries (tasft/inference/vllm_patch.py:172-196); here each sequence attends only
+ * within itself. `base` is read as for tasft_bsa_prefill_fwd except:
+ *   base.q / k / v / out   packed [total, H, D]; strides given as [1, H, token, D]: the
+ *                          first is never stepped (pass total*H*D), e.g. {T*H*D, D, H*D, 1}
+ *   base.B                 number of sequences; base.S = longest sequence (NB = ceil(S/block))
+ *   kept lists             [B, Hm, NB, NB] per sequence, as for the padded call
+ * Sequence b is rows [cu_seqlens[b], cu_seqlens[b+1]). bf16/fp16, block 64, D 64 or 128;
+ * anything else returns TASFT_ERR_UNSUPPORTED. */
+typedef struct {
+  tasft_prefill_args base;
+  const int32_t* cu_seqlens; /* device [B + 1], ascending, cu_seqlens[0] = 0 */
+  int32_t total;             /* cu_seqlens[B] */
+} tasft_prefill_varlen_args;
+TASFT_API int tasft_bsa_prefill_varlen_fwd(const tasft_prefill_varlen_args* args, tasft_stream_t stream);
+
 /* ------------------------------------------------------------------------- */
 /* Block-sparse decode (one query token per sequence), split-KV               */
 /* ------------------------------------------------------------------------- */

@@ -68,6 +68,10 @@ class PrefillArgs(C.Structure):
     ]
 
 
+class PrefillVarlenArgs(C.Structure):
+    _fields_ = [("base", PrefillArgs), ("cu_seqlens", vp), ("total", C.c_int32)]
+
+
 class DecodeArgs(C.Structure):
     _fields_ = [
         ("q", vp), ("k_cache", vp), ("v_cache", vp), ("out", vp),
@@ -129,6 +133,7 @@ SIGNATURES = {
     "tasft_mask_from_scores": ([C.POINTER(ThresholdArgs), vp], C.c_int),
     "tasft_mask_to_kept": ([C.POINTER(MaskArgs), vp], C.c_int),
     "tasft_bsa_prefill_fwd": ([C.POINTER(PrefillArgs), vp], C.c_int),
+    "tasft_bsa_prefill_varlen_fwd": ([C.POINTER(PrefillVarlenArgs), vp], C.c_int),
     "tasft_decode_workspace_size": ([C.c_int32] * 5, C.c_int64),
     "tasft_bsa_decode_fwd": ([C.POINTER(DecodeArgs), vp], C.c_int),
     "tasft_bsa_decode_combine": ([C.POINTER(CombineArgs), vp], C.c_int),

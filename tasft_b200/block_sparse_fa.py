@@ -148,6 +148,62 @@ class BlockSparseFlashAttention:
 
     __call__ = forward
 
+    def forward_varlen(
+        self,
+        q: torch.Tensor,
+        k: torch.Tensor,
+        v: torch.Tensor,
+        cu_seqlens: torch.Tensor,
+        max_seqlen: int,
+        block_mask: torch.Tensor | KeptBlocks,
+        *,
+        causal: bool = True,
+        out: torch.Tensor | None = None,
+        err: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        """Block-sparse attention over sequences of different lengths packed along the
+        token axis: q ``[T, Hq, D]``, k/v ``[T, Hk, D]``, ``cu_seqlens`` int32 ``[B + 1]``
+        (sequence b is rows ``cu_seqlens[b]:cu_seqlens[b+1]``), masks per sequence
+        ``[B, H, NB, NB]`` with ``NB = ceil(max_seqlen / block)``. Each sequence attends only
+        within itself -- unlike the reference's vLLM prefill, which flattens the batch into one
+        causal sequence (``tasft/inference/vllm_patch.py:172-196``). bf16/fp16, block 64."""
+        if q.ndim != 3 or k.ndim != 3 or k.shape != v.shape or k.shape[0] != q.shape[0] or \
+                k.shape[2] != q.shape[2] or q.shape[1] % max(k.shape[1], 1) != 0:
+            raise KernelError("varlen expects q [T, Hq, D] and k, v [T, Hk, D]",
+                              context={"q": list(q.shape), "k": list(k.shape), "v": list(v.shape)})
+        L.require_cuda(q, k, v, cu_seqlens)
+        T_, Hq, D = q.shape
+        Hk = k.shape[1]
+        B = cu_seqlens.numel() - 1
+        nb = math.ceil(max_seqlen / self.block_size)
+        kept = block_mask if isinstance(block_mask, KeptBlocks) else mask_to_kept(block_mask, causal)
+        if kept.idx.shape[0] != B or tuple(kept.idx.shape[2:]) != (nb, nb):
+            raise KernelError("block_mask shape mismatch for varlen",
+                              context={"expected": [B, "H", nb, nb], "got": list(kept.idx.shape)})
+        q = q.contiguous()
+        k = k.contiguous()
+        v = v.contiguous()
+        cu = cu_seqlens.to(torch.int32).contiguous()
+        if out is None:
+            out = torch.empty_like(q)
+        idx = kept.idx.contiguous()
+        cnt = kept.cnt.contiguous()
+
+        def packed(x):  # [T, H, D] seen as [1, H, T, D] (the batch stride is never stepped)
+            return L.I64x4(x.numel(), x.stride(1), x.stride(0), x.stride(2))
+
+        base = L.PrefillArgs(
+            q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), out=out.data_ptr(),
+            q_stride=packed(q), k_stride=packed(k), v_stride=packed(v), o_stride=packed(out),
+            B=B, Hq=Hq, Hk=Hk, S=int(max_seqlen), D=D, block=self.block_size, dtype=L.dtype_code(q),
+            causal=int(causal), scale=1.0 / math.sqrt(D), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(),
+            Hm=idx.shape[1], err=L.ptr(err), force_simt=0,
+        )
+        args = L.PrefillVarlenArgs(base=base, cu_seqlens=cu.data_ptr(), total=T_)
+        L.check(L.lib().tasft_bsa_prefill_varlen_fwd(args, L.stream_ptr(q.device)), "tasft_bsa_prefill_varlen_fwd",
+                shape=[B, Hq, Hk, T_, D], block=self.block_size)
+        return out
+
     def _validate_inputs(self, q, k, v, block_mask) -> None:
         if q.ndim != _EXPECTED_TENSOR_NDIM:
             raise KernelError(f"Expected 4D tensors [B, H, S, D], got q.ndim={q.ndim}",

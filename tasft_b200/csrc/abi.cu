@@ -23,7 +23,8 @@ void debug_log(const char* fmt, ...) {
 }
 int prefill_simt(const tasft_prefill_args& a, cudaStream_t st);
 // Returns TASFT_ERR_UNSUPPORTED when the tcgen05 kernel does not cover the shape.
-int prefill_tc(const tasft_prefill_args& a, cudaStream_t st);
+// `cu` (cu_seqlens, B + 1 entries) and `total` describe packed sequences; nullptr / 0 otherwise.
+int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu = nullptr, int total = 0);
 }  // namespace tasft
 
 using namespace tasft;
@@ -43,6 +44,19 @@ extern "C" int tasft_bsa_prefill_fwd(const tasft_prefill_args* ap, tasft_stream_
     if (rc != TASFT_ERR_UNSUPPORTED) return rc;
   }
   return prefill_simt(a, st);
+}
+
+extern "C" int tasft_bsa_prefill_varlen_fwd(const tasft_prefill_varlen_args* vp, tasft_stream_t stream) {
+  if (!vp || !vp->cu_seqlens) return TASFT_ERR_INVALID_ARG;
+  const tasft_prefill_args& a = vp->base;
+  if (!a.q || !a.k || !a.v || !a.out || !a.kept_idx || !a.kept_cnt) return TASFT_ERR_INVALID_ARG;
+  if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.S <= 0 || a.D <= 0 || a.Hm <= 0 || vp->total <= 0)
+    return TASFT_ERR_INVALID_ARG;
+  if (a.Hq % a.Hk != 0 || a.Hq % a.Hm != 0) return TASFT_ERR_INVALID_ARG;
+  if (a.q_stride[3] != 1 || a.k_stride[3] != 1 || a.v_stride[3] != 1 || a.o_stride[3] != 1)
+    return TASFT_ERR_INVALID_ARG;
+  // packed sequences run on the tensor-core kernel only (bf16/fp16, block 64, D 64/128)
+  return prefill_tc(a, reinterpret_cast<cudaStream_t>(stream), vp->cu_seqlens, vp->total);
 }
 
 extern "C" const char* tasft_status_string(int status) {

@@ -96,7 +96,9 @@ constexpr int kMufuPairs = 18;  // pairs 0..17 on MUFU ex2, 18..31 by the polyno
 struct Work {
   int b, hk, head[2], qbs[2];
   int valid[2];
-  int n;  // union list length; -1 = no more tiles
+  int n;     // union list length; -1 = no more tiles
+  int len;   // tokens of sequence b (S, or its cu_seqlens length when packed)
+  int row0;  // row of its first token in the K/V/Q/O tensors (0, or cu_seqlens[b] when packed)
 };
 
 template <int D>
@@ -120,8 +122,9 @@ struct Smem {
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
-// Tile id -> work. Ids run heavy (late) q-blocks first.
-__device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, int NB, int id) {
+// Tile id -> work. Ids run heavy (late) q-blocks first. With `cu` (packed sequences of
+// different lengths) q-blocks past a sequence's end are marked invalid.
+__device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, const int32_t* cu, int NB, int id) {
   const int grp = a.Hq / a.Hk;
   const int pairs = grp >= 2 ? (grp + 1) / 2 : 1;
   const int nbp = grp >= 2 ? NB : (NB + 1) / 2;
@@ -145,6 +148,14 @@ __device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, int NB,
     }
   }
   w.n = 0;
+  w.len = a.S;
+  w.row0 = 0;
+  if (cu) {
+    w.row0 = cu[w.b];
+    w.len = cu[w.b + 1] - w.row0;
+    const int nbs = (w.len + kBlk - 1) / kBlk;
+    for (int s = 0; s < 2; ++s) w.valid[s] = w.valid[s] && w.qbs[s] < nbs;
+  }
   return w;
 }
 
@@ -163,7 +174,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 template <int D, bool kF16>
 __global__ void __launch_bounds__(kThreads, 2)
     bsa_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                          const __grid_constant__ CUtensorMap tmv, const tasft_prefill_args a, const int NB) {
+                          const __grid_constant__ CUtensorMap tmv, const tasft_prefill_args a, const int NB,
+                          const int32_t* cu) {
   using L = Smem<D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -248,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         w.n = -1;
       } else {
         // ---- union of the two slots' kept lists (warp 0 only) ----
-        w = decode_tile(a, NB, tile);
+        w = decode_tile(a, cu, NB, tile);
         for (int i = lane; i < 2 * words; i += 32) bitmap[(i / words) * kWords + i % words] = 0;
         __syncwarp();
         for (int s = 0; s < 2; ++s) {
@@ -300,7 +312,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int s = 0; s < 2; ++s) {
             if (!w.valid[s]) continue;
             for (int c = 0; c < L::kChunks; ++c)
-              tc::tma_load_4d(sQ + c * 128 * 128 + s * 64 * 128, &tmq, c * 64, w.qbs[s] * kBlk, w.head[s], w.b,
+              tc::tma_load_4d(sQ + c * 128 * 128 + s * 64 * 128, &tmq, c * 64, w.row0 + w.qbs[s] * kBlk, w.head[s],
+                              cu ? 0 : w.b,
                               q_full);
           }
         }
@@ -311,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           uint8_t* dst = smem + L::kStageOff + L::kKOff + st * L::kKVTileBytes;
           mbar_arrive_expect_tx(&k_full[st], L::kKVTileBytes);
           for (int c = 0; c < L::kChunks; ++c)
-            tc::tma_load_4d(dst + c * 64 * 128, &tmk, c * 64, kb * kBlk, w.hk, w.b, &k_full[st]);
+            tc::tma_load_4d(dst + c * 64 * 128, &tmk, c * 64, w.row0 + kb * kBlk, w.hk, cu ? 0 : w.b, &k_full[st]);
           return true;
         };
         auto load_v = [&](int gi, int kb) -> bool {
@@ -320,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           uint8_t* dst = smem + L::kStageOff + L::kVOff + st * L::kKVTileBytes;
           mbar_arrive_expect_tx(&v_full[st], L::kKVTileBytes);
           for (int c = 0; c < L::kChunks; ++c)
-            tc::tma_load_4d(dst + c * 64 * 128, &tmv, c * 64, kb * kBlk, w.hk, w.b, &v_full[st]);
+            tc::tma_load_4d(dst + c * 64 * 128, &tmv, c * 64, w.row0 + kb * kBlk, w.hk, cu ? 0 : w.b, &v_full[st]);
           return true;
         };
         for (int j = 0; ok && j <= w.n && w.n > 0; ++j) {
@@ -441,8 +454,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t sraw[64];
         tc::tmem_ld64_sync(tS0 + (gi & 1) * 64 + lane_off, sraw);
         const int kbase = kb * kBlk;
-        // keys valid for this row: < S, and <= qpos when causal
-        int lim = a.S - kbase;
+        // keys valid for this row: inside its sequence, and <= qpos when causal (rows of
+        // the next packed sequence that a block overlaps are masked here)
+        int lim = w.len - kbase;
         if (a.causal) lim = min(lim, qpos - kbase + 1);
         if (!active) lim = 0;
         lim = max(0, min(lim, kBlk));
@@ -512,9 +526,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!warp_wait(o_final, u & 1)) { where = 14; ok = false; break; }
       tc::tc_fence_after();
       // ---- epilogue: O / l -> global (rows >= S and invalid slots are not stored) ----
-      const bool store = w.valid[slot] && qpos < a.S;
-      T* orow = reinterpret_cast<T*>(a.out) + w.b * a.o_stride[0] + (int64_t)w.head[slot] * a.o_stride[1] +
-                (int64_t)qpos * a.o_stride[2];
+      const bool store = w.valid[slot] && qpos < w.len;
+      T* orow = reinterpret_cast<T*>(a.out) + (cu ? 0 : w.b * a.o_stride[0]) + (int64_t)w.head[slot] * a.o_stride[1] +
+                (int64_t)(w.row0 + qpos) * a.o_stride[2];
       const float inv = (l > 0.f) ? 1.0f / l : 0.f;
       for (int c0 = 0; c0 < D; c0 += 32) {
         uint32_t o[32];
@@ -555,13 +569,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 template <int D, bool kF16>
-int launch_tc(const tasft_prefill_args& a, cudaStream_t st) {
+int launch_tc(const tasft_prefill_args& a, const int32_t* cu, int total, cudaStream_t st) {
   const int es = 2;
   const int NB = (a.S + kBlk - 1) / kBlk;
+  // packed sequences: one [1, H, total, D] tensor, rows offset by cu_seqlens in the kernel
+  const int mb = cu ? 1 : a.B, ms = cu ? total : a.S;
   CUtensorMap mq, mk, mv;
-  if (!make_tmap_bhsd(&mq, a.q, a.B, a.Hq, a.S, D, a.q_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
-  if (!make_tmap_bhsd(&mk, a.k, a.B, a.Hk, a.S, D, a.k_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
-  if (!make_tmap_bhsd(&mv, a.v, a.B, a.Hk, a.S, D, a.v_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
+  if (!make_tmap_bhsd(&mq, a.q, mb, a.Hq, ms, D, a.q_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
+  if (!make_tmap_bhsd(&mk, a.k, mb, a.Hk, ms, D, a.k_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
+  if (!make_tmap_bhsd(&mv, a.v, mb, a.Hk, ms, D, a.v_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
   const int grp = a.Hq / a.Hk;
   const int pairs = grp >= 2 ? (grp + 1) / 2 : 1;
   const int nbp = grp >= 2 ? NB : (NB + 1) / 2;
@@ -581,14 +597,14 @@ int launch_tc(const tasft_prefill_args& a, cudaStream_t st) {
   }
   if (grid > tiles) grid = tiles;
   if (debug_enabled()) debug_log("prefill_tc D=%d tiles=%lld grid=%lld smem=%d", D, (long long)tiles, (long long)grid, smem);
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB);
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB, cu);
   count_launch();
   return launch_status();
 }
 
 }  // namespace
 
-int prefill_tc(const tasft_prefill_args& a, cudaStream_t st) {
+int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu, int total) {
   if (a.block != kBlk) return TASFT_ERR_UNSUPPORTED;
   if (a.dtype != TASFT_BF16 && a.dtype != TASFT_F16) return TASFT_ERR_UNSUPPORTED;
   if (a.D != 64 && a.D != 128) return TASFT_ERR_UNSUPPORTED;
@@ -598,8 +614,8 @@ int prefill_tc(const tasft_prefill_args& a, cudaStream_t st) {
   if (!aligned16(a.out) || (a.o_stride[0] % 8) || (a.o_stride[1] % 8) || (a.o_stride[2] % 8))
     return TASFT_ERR_UNSUPPORTED;
   const bool f16 = a.dtype == TASFT_F16;
-  if (a.D == 128) return f16 ? launch_tc<128, true>(a, st) : launch_tc<128, false>(a, st);
-  return f16 ? launch_tc<64, true>(a, st) : launch_tc<64, false>(a, st);
+  if (a.D == 128) return f16 ? launch_tc<128, true>(a, cu, total, st) : launch_tc<128, false>(a, cu, total, st);
+  return f16 ? launch_tc<64, true>(a, cu, total, st) : launch_tc<64, false>(a, cu, total, st);
 }
 
 }  // namespace tasft
