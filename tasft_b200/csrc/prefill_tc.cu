@@ -69,29 +69,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair on the FMA pipe, to take load off the MUFU unit. Range reduction
-// x = j + f with j = round(x) obtained by adding 1.5 * 2^23 (so j sits in the low
-// mantissa bits of t), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients
-// were fitted for this kernel (least squares on the relative error over [-1/2, 1/2],
-// max relative error 7.5e-5, well under the bf16 rounding applied to P afterwards);
-// 2^j is added to the exponent field. Inputs are clamped at -125 so the exponent stays
-// normal.
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  x = f2(fmaxf(lo_f(x), -125.f), fmaxf(hi_f(x), -125.f));
-  const uint64_t t = add2(x, f2(kRound, kRound));
-  const uint64_t r = add2(t, f2(-kRound, -kRound));
-  const uint64_t f = fma2(r, f2(-1.f, -1.f), x);
-  uint64_t p = fma2(f2(0.05517049878835678f, 0.05517049878835678f), f,
-                    f2(0.24260851740837097f, 0.24260851740837097f));
-  p = fma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
-  p = fma2(p, f, f2(0.9999282360076904f, 0.9999282360076904f));
-  const uint32_t plo = (uint32_t)p + ((uint32_t)t << 23);
-  const uint32_t phi = (uint32_t)(p >> 32) + ((uint32_t)(t >> 32) << 23);
-  return ((uint64_t)phi << 32) | plo;
-}
-
-constexpr int kMufuPairs = 18;  // pairs 0..17 on MUFU ex2, 18..31 by the polynomial
 
 struct Work {
   int b, hk, head[2], qbs[2];
@@ -508,9 +485,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
             const uint64_t x2 = fma2(f2(sv[2 * c], sv[2 * c + 1]), sc2, nm2);  // s * scale - m
-            uint64_t p2;
-            if (c < kMufuPairs) p2 = f2(ex2(lo_f(x2)), ex2(hi_f(x2)));
-            else p2 = exp2_poly2(x2);
+            // all on MUFU ex2: measured faster than moving part of 2^x to the FMA pipe,
+            // which the packed arithmetic around it already keeps busy
+            const uint64_t p2 = f2(ex2(lo_f(x2)), ex2(hi_f(x2)));
             rs2 = add2(rs2, p2);
             pk[c] = kF16 ? tc::pack_f16x2(lo_f(p2), hi_f(p2)) : tc::pack_bf16x2(lo_f(p2), hi_f(p2));
           }
