@@ -14,8 +14,16 @@ stream; L2 is flushed (a 256 MiB write) before every timed step, outside the eve
 ``value`` = kept-block FLOPs of all ranks / max-over-ranks device time of the step
 ``mask -> kept lists -> tcgen05 prefill``. ``e2e`` = the same metric through
 ``BlockSparseFlashAttention.forward`` with pinned host inputs (H2D q, k, v, mask and D2H
-of the output inside the timed region). ``--impl reference`` times the CPU oracle (the
-restatement of the reference kernel) on the host cores instead.
+of the output inside the timed region; one call per sequence, copies and calls pipelined
+on two streams; the unpipelined time is reported beside it). ``--impl reference`` times
+the CPU oracle (the restatement of the reference kernel) on the host cores instead.
+
+Also on the line: ``roofline`` (prefill kernel vs measured bf16 peak), ``decode``
+(configs[2], HBM roofline; ``decode.paged`` the same over a 16-token paged cache),
+``gate`` (mask build replayed from a CUDA graph, HBM roofline), ``gate_target``
+(configs[4], tensor roofline), ``long_decode`` (configs[3] decode at KV 32768; with N > 1
+the cache is split by position over the ranks and the partials are all-gathered and
+merged), ``clocks`` (nvidia-smi sampled during the timed phases), ``cpu_baseline``.
 """
 from __future__ import annotations
 
