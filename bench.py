@@ -490,8 +490,11 @@ def run_ours(args):
     lmask = M.decode_mask(torch.rand(lc["B"], lc["Hk"], nbl, device=dev, generator=g), (kvl + 63) // 64,
                           lc["density"], nbl)
     lkept = T.KeptBlocks(*M.lists_from_mask(lmask))
+    ltiming = "CUDA graph replay"
     if ws > 1:
+        # eager: capturing the NCCL all-gather in a CUDA graph stalled the ranks here
         lstep = lambda: SH.long_context_decode(ql, kl_loc, vl_loc, kvl, lkept, lo)  # noqa: E731
+        ltiming = "eager calls incl. the NCCL all-gather"
     else:
         # one GPU: the step replayed from a CUDA graph, as a serving loop would run it (its
         # Python launch path takes longer than the ~20 us of kernels)
@@ -503,7 +506,7 @@ def run_ours(args):
                    "split": f"KV positions over {ws} rank(s); partials all-gathered + log-sum-exp combine"
                             if ws > 1 else "one GPU",
                    "scaling": "strong", "ms_per_token": round(ms_l, 4),
-                   "timing": "CUDA graph replay" if ws == 1 else "eager calls incl. the NCCL all-gather",
+                   "timing": ltiming,
                    "tok_s": round(lc["B"] / (ms_l * 1e-3), 1)}
     del kl_loc, vl_loc
 

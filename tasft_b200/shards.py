@@ -67,16 +67,21 @@ def local_kv_len(kv_len: torch.Tensor, lo: int, hi: int, block: int) -> torch.Te
 
 def gather_partials(part_o: torch.Tensor, part_ml: torch.Tensor, group=None):
     """All-gather ``o [B,Hq,D]`` and ``ml [B,Hq,2]`` (fp32) from every rank of ``group``:
-    returns ``[G,B,Hq,D]`` and ``[G,B,Hq,2]`` in rank order."""
+    returns ``[G,B,Hq,D]`` and ``[G,B,Hq,2]`` in rank order. Both travel in ONE collective
+    (a flat ``[o | ml]`` buffer per rank): the exchange is a few KB, so its cost is the
+    collective's latency, paid once."""
     import torch.distributed as dist  # noqa: PLC0415
 
     g = dist.get_world_size(group)
-    po = torch.empty((g, *part_o.shape), dtype=part_o.dtype, device=part_o.device)
-    pm = torch.empty((g, *part_ml.shape), dtype=part_ml.dtype, device=part_ml.device)
-    # into views of one preallocated tensor per kind (works on NCCL and on gloo)
-    dist.all_gather(list(po.unbind(0)), part_o.contiguous(), group=group)
-    dist.all_gather(list(pm.unbind(0)), part_ml.contiguous(), group=group)
-    return po, pm
+    no, nm = part_o.numel(), part_ml.numel()
+    flat = torch.cat([part_o.reshape(-1), part_ml.reshape(-1)])
+    out = torch.empty(g * (no + nm), dtype=flat.dtype, device=flat.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, flat, group=group)
+    else:  # gloo takes the list form
+        dist.all_gather(list(out.view(g, no + nm).unbind(0)), flat, group=group)
+    rows = out.view(g, no + nm)
+    return rows[:, :no].reshape(g, *part_o.shape), rows[:, no:].reshape(g, *part_ml.shape)
 
 
 def long_context_decode(
