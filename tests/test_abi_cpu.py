@@ -93,3 +93,42 @@ def test_check_raises_kernel_error():
         L.check(-1, "x")
     with pytest.raises(KernelError):
         L.check(-2, "x")
+
+
+# ctypes mirrors of the header's structs: every field's offset and every struct's size,
+# as gcc lays them out from include/tasft_b200.h (a drift would corrupt calls silently)
+_STRUCTS = {
+    "tasft_gate_args": "GateArgs", "tasft_threshold_args": "ThresholdArgs", "tasft_mask_args": "MaskArgs",
+    "tasft_prefill_args": "PrefillArgs", "tasft_prefill_varlen_args": "PrefillVarlenArgs",
+    "tasft_decode_args": "DecodeArgs", "tasft_paged_decode_args": "PagedDecodeArgs",
+    "tasft_combine_args": "CombineArgs", "tasft_target_args": "TargetArgs", "tasft_loss_args": "LossArgs",
+    "tasft_gate_bwd_args": "GateBwdArgs",
+}
+
+
+def test_struct_layouts_match_header(tmp_path):
+    import ctypes as C  # noqa: PLC0415
+    import shutil  # noqa: PLC0415
+    import subprocess  # noqa: PLC0415
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    lines = ["#include <stddef.h>", "#include <stdio.h>", f'#include "{HEADER}"', "int main(void) {"]
+    for cname, pyname in _STRUCTS.items():
+        cls = getattr(L, pyname)
+        lines.append(f'  printf("{pyname} size %zu\\n", sizeof({cname}));')
+        for field, _ in cls._fields_:
+            lines.append(f'  printf("{pyname}.{field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-std=c11", "-o", str(exe), str(src)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                                check=True).stdout.splitlines())
+    for pyname in _STRUCTS.values():
+        cls = getattr(L, pyname)
+        assert int(got[f"{pyname} size"]) == C.sizeof(cls), pyname
+        for field, _ in cls._fields_:
+            assert int(got[f"{pyname}.{field}"]) == getattr(cls, field).offset, f"{pyname}.{field}"
