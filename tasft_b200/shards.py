@@ -40,6 +40,44 @@ def assign_units(weights, world: int) -> list[list[int]]:
     return [sorted(x) for x in out]
 
 
+def unit_weights(kept: KeptBlocks, hk: int) -> torch.Tensor:
+    """Kept blocks per prefill unit (sequence, kv-head), ``[B * Hk]`` in unit order
+    ``b * Hk + hk``: the work measure ``assign_units`` balances."""
+    cnt = kept.cnt  # [B, Hm, NB]
+    B, hm = cnt.shape[0], cnt.shape[1]
+    return cnt.reshape(B, hk, hm // hk, -1).sum(dim=(2, 3)).reshape(-1)
+
+
+def prefill_units(kern, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kept: KeptBlocks, units,
+                  causal: bool = True) -> torch.Tensor:
+    """Prefill of the (sequence, kv-head) units ``units`` only (ids ``b * Hk + hk``), as
+    one call over a batch of units: returns ``[len(units), Hq/Hk, S, D]``, the q-heads of
+    each unit's group. A rank of a sharded prefill passes the units ``assign_units`` gave
+    it; the tensors may be the full batch or just those units' slices gathered by the
+    caller (then ``units`` are indices into that smaller batch)."""
+    Hk = k.shape[1]
+    grp = q.shape[1] // Hk
+    hm = kept.idx.shape[1]
+    mg = hm // Hk  # list heads per kv-head (1: kv-head lists, grp: per-q-head lists)
+    ids = torch.as_tensor(list(units), dtype=torch.long, device=q.device)
+    b, h = ids // Hk, ids % Hk
+    hq = (h[:, None] * grp + torch.arange(grp, device=q.device)[None, :])  # [U, grp]
+    hl = (h[:, None] * mg + torch.arange(mg, device=q.device)[None, :])    # [U, mg]
+    qu = q[b[:, None], hq]              # [U, grp, S, D]
+    ku = k[b, h].unsqueeze(1)           # [U, 1, S, D]
+    vu = v[b, h].unsqueeze(1)
+    ku_kept = KeptBlocks(kept.idx[b[:, None], hl].contiguous(), kept.cnt[b[:, None], hl].contiguous())
+    return kern.forward(qu, ku, vu, ku_kept, causal=causal)
+
+
+def scatter_units(out: torch.Tensor, parts: torch.Tensor, units, Hk: int) -> None:
+    """Write unit outputs ``[U, grp, S, D]`` back into the full ``[B, Hq, S, D]`` tensor."""
+    grp = out.shape[1] // Hk
+    for i, u in enumerate(units):
+        b, h = divmod(int(u), Hk)
+        out[b, h * grp:(h + 1) * grp] = parts[i]
+
+
 def block_range(nb: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous KV-block range ``[lo, hi)`` of ``rank`` when ``nb`` blocks split over ``world``."""
     base, extra = divmod(nb, world)
@@ -115,4 +153,5 @@ def long_context_decode(
     return decode_combine(ao, am, q.dtype)
 
 
-__all__ = ["assign_units", "block_range", "gather_partials", "local_kept", "local_kv_len", "long_context_decode"]
+__all__ = ["assign_units", "block_range", "gather_partials", "local_kept", "local_kv_len", "long_context_decode",
+           "prefill_units", "scatter_units", "unit_weights"]

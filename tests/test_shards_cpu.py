@@ -113,3 +113,11 @@ def test_split_kv_decode_over_gloo_matches_unsplit(world):
     q, kc, vc, kv_len, idx, cnt = _inputs()
     ref = O.bsa_decode(q, kc, vc, kv_len, idx, cnt, 64)
     torch.testing.assert_close(got, ref.float(), atol=1e-5, rtol=1e-5)
+
+
+def test_unit_weights_sum_kept_blocks_per_kv_head():
+    cnt = torch.tensor([[[1, 2], [3, 4], [5, 6], [7, 8]]], dtype=torch.int32)  # B=1, Hm=4 (q-heads), NB=2
+    kept = KeptBlocks(torch.zeros(1, 4, 2, 2, dtype=torch.int32), cnt)
+    assert SH.unit_weights(kept, 2).tolist() == [1 + 2 + 3 + 4, 5 + 6 + 7 + 8]
+    kv = KeptBlocks(torch.zeros(1, 2, 2, 2, dtype=torch.int32), cnt[:, :2])
+    assert SH.unit_weights(kv, 2).tolist() == [3, 7]

@@ -85,3 +85,24 @@ def test_nccl_two_ranks_match_unsplit():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert max(errs.values()) <= 2e-2
+
+
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_sharded_prefill_units_equal_full_batch(world):
+    """LPT-sharded prefill: every rank runs its (sequence, kv-head) units; scattered back,
+    the result is exactly the one-call prefill's."""
+    g = torch.Generator(device=DEV).manual_seed(31)
+    B, Hq, Hk, S, D = 2, 32, 8, 1024, 128
+    q = torch.randn(B, Hq, S, D, device=DEV, generator=g).bfloat16()
+    k = torch.randn(B, Hk, S, D, device=DEV, generator=g).bfloat16()
+    v = torch.randn(B, Hk, S, D, device=DEV, generator=g).bfloat16()
+    mask = M.prefill_mask(torch.rand(B, Hk, S // 64, S // 64, device=DEV, generator=g), 0.2)
+    kern = T.BlockSparseFlashAttention()
+    kept = T.mask_to_kept(mask, True)
+    full = kern.forward(q, k, v, kept)
+    parts = SH.assign_units(SH.unit_weights(kept, Hk), world)
+    out = torch.zeros_like(full)
+    for units in parts:
+        if units:
+            SH.scatter_units(out, SH.prefill_units(kern, q, k, v, kept, units), units, Hk)
+    assert torch.equal(out, full)
