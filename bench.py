@@ -492,8 +492,11 @@ def run_ours(args):
     lkept = T.KeptBlocks(*M.lists_from_mask(lmask))
     ltiming = "CUDA graph replay"
     if ws > 1:
-        # eager: capturing the NCCL all-gather in a CUDA graph stalled the ranks here
-        lstep = lambda: SH.long_context_decode(ql, kl_loc, vl_loc, kvl, lkept, lo)  # noqa: E731
+        # eager (capturing the NCCL all-gather in a CUDA graph stalled the ranks here), with
+        # the decoder's buffers and this rank's rebased kept lists kept across steps
+        dec = SH.SplitKVDecoder(lc["B"], lc["Hq"], lc["Hk"], lc["D"], dev)
+        lloc = dec.local(lkept, lo, hi - lo)
+        lstep = lambda: dec(ql, kl_loc, vl_loc, kvl, lkept, lo, local=lloc)  # noqa: E731
         ltiming = "eager calls incl. the NCCL all-gather"
     else:
         # one GPU: the step replayed from a CUDA graph, as a serving loop would run it (its

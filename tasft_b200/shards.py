@@ -153,5 +153,49 @@ def long_context_decode(
     return decode_combine(ao, am, q.dtype)
 
 
+class SplitKVDecoder:
+    """``long_context_decode`` with its buffers kept across calls (workspace, partials, the
+    gather buffer), for a serving loop that decodes one token per step. ``local`` lets the
+    caller pass the rank's rebased kept lists when they did not change since the last step."""
+
+    def __init__(self, B: int, Hq: int, Hk: int, D: int, device, group=None, block: int = 64,
+                 num_splits: int = 0) -> None:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        from tasft_b200.decode import DecodeWorkspace  # noqa: PLC0415
+
+        self.group, self.block, self.num_splits = group, block, num_splits
+        self.world = dist.get_world_size(group)
+        self.nccl = dist.get_backend(group) == "nccl"
+        self.ws = DecodeWorkspace(B, Hq, Hk, D, max(num_splits, 16), device)
+        self.no, self.nm = B * Hq * D, B * Hq * 2
+        self.flat = torch.empty(self.no + self.nm, dtype=torch.float32, device=device)
+        self.po = self.flat[: self.no].view(B, Hq, D)
+        self.pm = self.flat[self.no:].view(B, Hq, 2)
+        self.gathered = torch.empty(self.world * (self.no + self.nm), dtype=torch.float32, device=device)
+        self.shape = (B, Hq, D)
+
+    def local(self, kept: KeptBlocks, block_lo: int, nloc: int) -> KeptBlocks:
+        return local_kept(kept, block_lo, block_lo + nloc)
+
+    def __call__(self, q, k_local, v_local, kv_len, kept: KeptBlocks, block_lo: int,
+                 local: KeptBlocks | None = None) -> torch.Tensor:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        from tasft_b200.decode import bsa_decode, decode_combine  # noqa: PLC0415
+
+        nloc = k_local.shape[2] // self.block
+        kl = local if local is not None else local_kept(kept, block_lo, block_lo + nloc)
+        bsa_decode(q, k_local, v_local, local_kv_len(kv_len, block_lo, block_lo + nloc, self.block), kl, self.block,
+                   num_splits=self.num_splits, workspace=self.ws, partials=(self.po, self.pm))
+        if self.nccl:
+            dist.all_gather_into_tensor(self.gathered, self.flat, group=self.group)
+        else:
+            dist.all_gather(list(self.gathered.view(self.world, -1).unbind(0)), self.flat, group=self.group)
+        rows = self.gathered.view(self.world, self.no + self.nm)
+        return decode_combine(rows[:, : self.no].view(self.world, *self.shape),
+                              rows[:, self.no:].view(self.world, self.shape[0], self.shape[1], 2), q.dtype)
+
+
 __all__ = ["assign_units", "block_range", "gather_partials", "local_kept", "local_kv_len", "long_context_decode",
-           "prefill_units", "scatter_units", "unit_weights"]
+           "prefill_units", "scatter_units", "unit_weights", "SplitKVDecoder"]

@@ -106,3 +106,43 @@ def test_sharded_prefill_units_equal_full_batch(world):
         if units:
             SH.scatter_units(out, SH.prefill_units(kern, q, k, v, kept, units), units, Hk)
     assert torch.equal(out, full)
+
+
+def _rank_decoder(rank, world, port, res):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist  # noqa: PLC0415
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        q, kc, vc, kv_len, kept = _inputs(dev)
+        lo, hi = SH.block_range(kc.shape[2] // 64, rank, world)
+        dec = SH.SplitKVDecoder(q.shape[0], q.shape[1], kc.shape[1], q.shape[2], dev)
+        kl, vl = kc[:, :, lo * 64 : hi * 64].contiguous(), vc[:, :, lo * 64 : hi * 64].contiguous()
+        loc = dec.local(kept, lo, hi - lo)
+        ref = T.bsa_decode(q, kc, vc, kv_len, kept, 64)
+        errs = [(dec(q, kl, vl, kv_len, kept, lo, local=loc).float() - ref.float()).abs().max().item()
+                for _ in range(3)]  # buffers reused across calls
+        res.put((rank, max(errs)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_split_kv_decoder_reuses_buffers_two_ranks():
+    import torch.multiprocessing as mp  # noqa: PLC0415
+
+    ctx = mp.get_context("spawn")
+    res = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_rank_decoder, args=(r, 2, port, res)) for r in range(2)]
+    for p in procs:
+        p.start()
+    errs = dict(res.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert max(errs.values()) <= 2e-2
