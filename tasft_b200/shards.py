@@ -78,6 +78,30 @@ def scatter_units(out: torch.Tensor, parts: torch.Tensor, units, Hk: int) -> Non
         out[b, h * grp:(h + 1) * grp] = parts[i]
 
 
+def qblock_ranges(kept: KeptBlocks, world: int) -> list[tuple[int, int]]:
+    """Contiguous q-block ranges ``[lo, hi)`` with about equal kept work each, for a
+    prefill with too few (sequence, kv-head) units to go around (one long sequence): the
+    boundaries cut the cumulative kept-block count summed over batch and heads."""
+    per_q = kept.cnt.sum(dim=tuple(range(kept.cnt.ndim - 1))).double().cpu()  # [NB], host-side planning
+    cum = torch.cumsum(per_q, 0)
+    total = float(cum[-1]) if cum.numel() else 0.0
+    nb = per_q.numel()
+    cuts = [0]
+    for r in range(1, world):
+        c = int(torch.searchsorted(cum, torch.tensor(total * r / world, dtype=cum.dtype)).item()) + 1
+        cuts.append(min(max(c, cuts[-1]), nb))
+    cuts.append(nb)
+    return [(cuts[r], cuts[r + 1]) for r in range(world)]
+
+
+def restrict_qblocks(kept: KeptBlocks, lo: int, hi: int) -> KeptBlocks:
+    """The prefill lists with every q-block outside ``[lo, hi)`` emptied: a prefill on them
+    computes only those q-blocks (the other rows come out as zeros)."""
+    nb = kept.cnt.shape[-1]
+    inside = (torch.arange(nb, device=kept.cnt.device) >= lo) & (torch.arange(nb, device=kept.cnt.device) < hi)
+    return KeptBlocks(kept.idx, torch.where(inside, kept.cnt, torch.zeros_like(kept.cnt)).contiguous())
+
+
 def block_range(nb: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous KV-block range ``[lo, hi)`` of ``rank`` when ``nb`` blocks split over ``world``."""
     base, extra = divmod(nb, world)
@@ -198,4 +222,5 @@ class SplitKVDecoder:
 
 
 __all__ = ["assign_units", "block_range", "gather_partials", "local_kept", "local_kv_len", "long_context_decode",
-           "prefill_units", "scatter_units", "unit_weights", "SplitKVDecoder"]
+           "prefill_units", "qblock_ranges", "restrict_qblocks", "scatter_units", "unit_weights",
+           "SplitKVDecoder"]

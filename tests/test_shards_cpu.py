@@ -121,3 +121,17 @@ def test_unit_weights_sum_kept_blocks_per_kv_head():
     assert SH.unit_weights(kept, 2).tolist() == [1 + 2 + 3 + 4, 5 + 6 + 7 + 8]
     kv = KeptBlocks(torch.zeros(1, 2, 2, 2, dtype=torch.int32), cnt[:, :2])
     assert SH.unit_weights(kv, 2).tolist() == [3, 7]
+
+
+def test_qblock_ranges_partition_and_balance():
+    nb = 64
+    cnt = torch.arange(1, nb + 1, dtype=torch.int32).view(1, 1, nb).expand(1, 4, nb)  # causal-like growth
+    kept = KeptBlocks(torch.zeros(1, 4, nb, nb, dtype=torch.int32), cnt.contiguous())
+    for world in (1, 2, 3, 8):
+        rs = SH.qblock_ranges(kept, world)
+        assert rs[0][0] == 0 and rs[-1][1] == nb and all(rs[i][1] == rs[i + 1][0] for i in range(world - 1))
+        work = [int(cnt[0, 0, lo:hi].sum()) * 4 for lo, hi in rs]
+        assert max(work) <= sum(work) / world + 4 * nb  # within one q-block of the mean
+    r = SH.restrict_qblocks(kept, 10, 20)
+    assert r.cnt[0, 0, :10].eq(0).all() and r.cnt[0, 0, 20:].eq(0).all()
+    assert torch.equal(r.cnt[0, 0, 10:20], cnt[0, 0, 10:20])

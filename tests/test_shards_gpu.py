@@ -146,3 +146,24 @@ def test_split_kv_decoder_reuses_buffers_two_ranks():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert max(errs.values()) <= 2e-2
+
+
+@pytest.mark.parametrize("world", [3, 8])
+def test_long_prefill_qblock_ranges_sum_to_full(world):
+    """One long sequence, 4 kv-heads: ranks split the q-blocks by kept work; each rank's
+    rows outside its range are zero, so the ranks' outputs sum to the one-call prefill."""
+    g = torch.Generator(device=DEV).manual_seed(32)
+    B, Hq, Hk, S, D = 1, 28, 4, 8192, 128
+    q = torch.randn(B, Hq, S, D, device=DEV, generator=g).bfloat16()
+    k = torch.randn(B, Hk, S, D, device=DEV, generator=g).bfloat16()
+    v = torch.randn(B, Hk, S, D, device=DEV, generator=g).bfloat16()
+    mask = M.prefill_mask(torch.rand(B, Hk, S // 64, S // 64, device=DEV, generator=g), 0.1)
+    kern = T.BlockSparseFlashAttention()
+    kept = T.mask_to_kept(mask, True)
+    full = kern.forward(q, k, v, kept)
+    acc = torch.zeros_like(full, dtype=torch.float32)
+    for lo, hi in SH.qblock_ranges(kept, world):
+        part = kern.forward(q, k, v, SH.restrict_qblocks(kept, lo, hi))
+        assert part[:, :, : lo * 64].eq(0).all() and part[:, :, hi * 64:].eq(0).all()
+        acc += part.float()
+    assert torch.equal(acc.to(full.dtype), full)
