@@ -1,13 +1,14 @@
-// AttnGate mask builder: fused block pooling + gate projection, pair scores,
-// threshold and kept-block list emission.
+// AttnGate mask builder: block pooling, gate projection, pair scores, threshold and
+// kept-block list emission.
 //
 // Reference: tasft/modules/attn_gate.py:351-485 (AttnGate._pool_to_blocks / forward).
 // The reference materialises every (q-block, k-block) pair [q_i; k_j] and runs
 // Linear(2D->hid) on it. Here the first layer is split by linearity:
 //   W_in [q_i; k_j] + b = (W_q q_i + b) + W_k k_j =: a_i + c_j
-// so a_i and c_j are computed once per block while pooling (one HBM pass over Q and
-// K), and the pair kernel only evaluates w_out . relu(a_i + c_j). Same maths; the fp32
-// summation order differs from the reference's single 2D-long dot product.
+// so a_i and c_j are computed once per block (one HBM pass over Q and K pools them; a
+// small kernel projects the means), and the pair kernel only evaluates
+// w_out . relu(a_i + c_j). Same maths; the fp32 summation order differs from the
+// reference's single 2D-long dot product.
 #include "common.cuh"
 
 namespace tasft {

@@ -22,6 +22,9 @@
 //   warps 2-5  softmax: one thread per row; tcgen05.ld S, mask, online max with a lazy
 //              O rescale (only when the max grows by > 2^8), p = 2^x, tcgen05.st P (bf16)
 //              back into TMEM, epilogue O / l, which overlaps the next tile's loads.
+// Packed sequences (cu_seqlens, the vLLM prefill layout) use the same kernel: the tensors
+// are one [1, H, total, D] map, every row coordinate is offset by its sequence's start,
+// and keys and stores are bounded by the sequence's own length.
 // Every mbarrier phase is indexed by a global block counter or by the CTA's tile counter,
 // and every wait is arranged so the waiter is at most one phase behind (a parity wait
 // cannot tell phase k from phase k + 2). Every wait is bounded (TASFT_DEVERR_TIMEOUT).
