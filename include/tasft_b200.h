@@ -161,8 +161,9 @@ TASFT_API int tasft_bsa_prefill_fwd(const tasft_prefill_args* args, tasft_stream
  *                          first is never stepped (pass total*H*D), e.g. {T*H*D, D, H*D, 1}
  *   base.B                 number of sequences; base.S = longest sequence (NB = ceil(S/block))
  *   kept lists             [B, Hm, NB, NB] per sequence, as for the padded call
- * Sequence b is rows [cu_seqlens[b], cu_seqlens[b+1]). bf16/fp16, block 64, D 64 or 128;
- * anything else returns TASFT_ERR_UNSUPPORTED. */
+ * Sequence b is rows [cu_seqlens[b], cu_seqlens[b+1]). Same dtypes, blocks and head dims
+ * as tasft_bsa_prefill_fwd (tensor cores for bf16/fp16, block 64, D 64/128; the CUDA-core
+ * kernel otherwise, or with base.force_simt). */
 typedef struct {
   tasft_prefill_args base;
   const int32_t* cu_seqlens; /* device [B + 1], ascending, cu_seqlens[0] = 0 */

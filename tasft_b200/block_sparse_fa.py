@@ -166,7 +166,8 @@ class BlockSparseFlashAttention:
         (sequence b is rows ``cu_seqlens[b]:cu_seqlens[b+1]``), masks per sequence
         ``[B, H, NB, NB]`` with ``NB = ceil(max_seqlen / block)``. Each sequence attends only
         within itself -- unlike the reference's vLLM prefill, which flattens the batch into one
-        causal sequence (``tasft/inference/vllm_patch.py:172-196``). bf16/fp16, block 64."""
+        causal sequence (``tasft/inference/vllm_patch.py:172-196``). Every dtype and block
+        size of ``forward``."""
         if q.ndim != 3 or k.ndim != 3 or k.shape != v.shape or k.shape[0] != q.shape[0] or \
                 k.shape[2] != q.shape[2] or q.shape[1] % max(k.shape[1], 1) != 0:
             raise KernelError("varlen expects q [T, Hq, D] and k, v [T, Hk, D]",
@@ -197,7 +198,7 @@ class BlockSparseFlashAttention:
             q_stride=packed(q), k_stride=packed(k), v_stride=packed(v), o_stride=packed(out),
             B=B, Hq=Hq, Hk=Hk, S=int(max_seqlen), D=D, block=self.block_size, dtype=L.dtype_code(q),
             causal=int(causal), scale=1.0 / math.sqrt(D), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(),
-            Hm=idx.shape[1], err=L.ptr(err), force_simt=0,
+            Hm=idx.shape[1], err=L.ptr(err), force_simt=int(self.force_simt),
         )
         args = L.PrefillVarlenArgs(base=base, cu_seqlens=cu.data_ptr(), total=T_)
         L.check(L.lib().tasft_bsa_prefill_varlen_fwd(args, L.stream_ptr(q.device)), "tasft_bsa_prefill_varlen_fwd",

@@ -21,7 +21,7 @@ void debug_log(const char* fmt, ...) {
   std::fprintf(stderr, "\n");
   va_end(ap);
 }
-int prefill_simt(const tasft_prefill_args& a, cudaStream_t st);
+int prefill_simt(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu = nullptr);
 // Returns TASFT_ERR_UNSUPPORTED when the tcgen05 kernel does not cover the shape.
 // `cu` (cu_seqlens, B + 1 entries) and `total` describe packed sequences; nullptr / 0 otherwise.
 int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu = nullptr, int total = 0);
@@ -55,8 +55,13 @@ extern "C" int tasft_bsa_prefill_varlen_fwd(const tasft_prefill_varlen_args* vp,
   if (a.Hq % a.Hk != 0 || a.Hq % a.Hm != 0) return TASFT_ERR_INVALID_ARG;
   if (a.q_stride[3] != 1 || a.k_stride[3] != 1 || a.v_stride[3] != 1 || a.o_stride[3] != 1)
     return TASFT_ERR_INVALID_ARG;
-  // packed sequences run on the tensor-core kernel only (bf16/fp16, block 64, D 64/128)
-  return prefill_tc(a, reinterpret_cast<cudaStream_t>(stream), vp->cu_seqlens, vp->total);
+  if (a.block != 32 && a.block != 64 && a.block != 128) return TASFT_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (!a.force_simt) {
+    const int rc = prefill_tc(a, st, vp->cu_seqlens, vp->total);
+    if (rc != TASFT_ERR_UNSUPPORTED) return rc;
+  }
+  return prefill_simt(a, st, vp->cu_seqlens);
 }
 
 extern "C" const char* tasft_status_string(int status) {

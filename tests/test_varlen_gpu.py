@@ -59,3 +59,27 @@ def test_varlen_fp16_noncausal_rows_isolated():
         q[s0:s0 + n].transpose(0, 1).float(), k[s0:s0 + n].transpose(0, 1).float().repeat_interleave(2, 0),
         v[s0:s0 + n].transpose(0, 1).float().repeat_interleave(2, 0))
     assert (out[s0:s0 + n].transpose(0, 1).float() - ref).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("dtype,block,force_simt", [(torch.float32, 64, False), (torch.float32, 32, False),
+                                                      (torch.float32, 128, False), (torch.bfloat16, 64, True)])
+def test_varlen_cuda_core_kernel_equals_per_sequence(dtype, block, force_simt):
+    lens = [90, 300, 33]
+    g = torch.Generator(device=DEV).manual_seed(7)
+    Hq, Hk, D = 4, 2, 64
+    tot = sum(lens)
+    q = torch.randn(tot, Hq, D, device=DEV, generator=g).to(dtype)
+    k = torch.randn(tot, Hk, D, device=DEV, generator=g).to(dtype)
+    v = torch.randn(tot, Hk, D, device=DEV, generator=g).to(dtype)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device=DEV)
+    nb = math.ceil(max(lens) / block)
+    mask = torch.rand(len(lens), Hk, nb, nb, device=DEV, generator=g) < 0.6
+    mask |= torch.eye(nb, dtype=torch.bool, device=DEV)
+    kern = T.BlockSparseFlashAttention(block_size=block)
+    kern.force_simt = force_simt
+    out = kern.forward_varlen(q, k, v, cu, max(lens), mask)
+    for b, n in enumerate(lens):
+        s0, nbs = int(cu[b]), math.ceil(n / block)
+        ref = kern.forward(q[s0:s0 + n].transpose(0, 1).unsqueeze(0), k[s0:s0 + n].transpose(0, 1).unsqueeze(0),
+                           v[s0:s0 + n].transpose(0, 1).unsqueeze(0), mask[b:b + 1, :, :nbs, :nbs].contiguous())
+        assert torch.equal(out[s0:s0 + n], ref[0].transpose(0, 1)), f"sequence {b}"
