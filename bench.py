@@ -557,12 +557,24 @@ def run_only(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    if args.only == "decode":
+    if args.only in ("decode", "paged"):
         qd, kc, vc, kv_len, kept = make_decode_inputs(1237, dev)
         splits = T.decode.default_splits(DEC["B"], DEC["Hk"], float(kept.cnt.float().mean().item()))
         wsp = T.DecodeWorkspace(DEC["B"], DEC["Hq"], DEC["Hk"], DEC["D"], splits, dev)
+        if args.only == "paged":  # the same cache as 16-token pages in a shuffled pool
+            pg, mp = 16, DEC["L"] // 16
+            table = torch.randperm(DEC["B"] * mp, device=dev).to(torch.int32).view(DEC["B"], mp)
+            kp = torch.empty(DEC["B"] * mp, pg, DEC["Hk"], DEC["D"], device=dev, dtype=kc.dtype)
+            vp = torch.empty_like(kp)
+            shape = (-1, pg, DEC["Hk"], DEC["D"])
+            kp[table.flatten().long()] = kc.view(DEC["B"], DEC["Hk"], mp, pg, DEC["D"]).permute(0, 2, 3, 1, 4).reshape(shape)
+            vp[table.flatten().long()] = vc.view(DEC["B"], DEC["Hk"], mp, pg, DEC["D"]).permute(0, 2, 3, 1, 4).reshape(shape)
+            del kc, vc
         for _ in range(args.steps):
-            T.bsa_decode(qd, kc, vc, kv_len, kept, DEC["block"], num_splits=splits, workspace=wsp)
+            if args.only == "paged":
+                T.bsa_decode_paged(qd, kp, vp, table, kv_len, kept, DEC["block"], num_splits=splits, workspace=wsp)
+            else:
+                T.bsa_decode(qd, kc, vc, kv_len, kept, DEC["block"], num_splits=splits, workspace=wsp)
     else:
         q, k, v, mask, gate = make_prefill_inputs(1236, dev)
         kern = T.BlockSparseFlashAttention(block_size=CFG["block"])
@@ -587,7 +599,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
-    ap.add_argument("--only", choices=["prefill", "decode", "gate", "target"],
+    ap.add_argument("--only", choices=["prefill", "decode", "paged", "gate", "target"],
                     help="profiling driver: run `--steps` launches of one kernel family, print nothing else")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
