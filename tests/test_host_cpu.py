@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import oracle as O
-from tasft_b200 import AttnGate, BlockSparseFlashAttention, KernelBackend, KernelError, ValidationError
+from tasft_b200 import AttnGate, BlockSparseFlashAttention, KernelBackend, KernelError, KeptBlocks, ValidationError
 from tasft_b200 import masks as M
 
 
@@ -179,3 +179,38 @@ def test_prefill_flops_accounting():
     m = M.prefill_mask(s, 0.2)
     flops = int(m.sum()) * 4 * 4 * 64 * 64 * 128  # x4 q-heads per kv-head
     assert math.isclose(flops / 1e9, 113.8, rel_tol=2e-3)
+
+
+class TestNewEntryPointsFailLoudly:
+    """The varlen prefill, paged decode and split-KV helpers reject bad input on the host
+    (no CPU fallback: CPU tensors raise, shape errors raise before any launch)."""
+
+    def test_varlen_shape_and_device_errors(self):
+        kern = BlockSparseFlashAttention()
+        q = torch.randn(100, 4, 64)
+        cu = torch.tensor([0, 100], dtype=torch.int32)
+        mask = torch.ones(1, 2, 2, 2, dtype=torch.bool)
+        with pytest.raises(KernelError):
+            kern.forward_varlen(q, torch.randn(100, 3, 64), torch.randn(100, 3, 64), cu, 100, mask)  # 4 % 3
+        with pytest.raises(KernelError):
+            kern.forward_varlen(q.unsqueeze(0), q, q, cu, 100, mask)  # not [T, H, D]
+        with pytest.raises(KernelError, match="CUDA"):
+            kern.forward_varlen(q, torch.randn(100, 2, 64), torch.randn(100, 2, 64), cu, 100, mask)
+
+    def test_paged_decode_errors(self):
+        import tasft_b200 as T  # noqa: PLC0415
+
+        q = torch.randn(2, 8, 64)
+        pages = torch.randn(10, 16, 2, 64)
+        table = torch.zeros(2, 4, dtype=torch.int32)
+        kept = KeptBlocks(torch.zeros(2, 2, 1, dtype=torch.int32), torch.ones(2, 2, dtype=torch.int32))
+        with pytest.raises(KernelError, match="CUDA"):
+            T.bsa_decode_paged(q, pages, pages, table, torch.full((2,), 64, dtype=torch.int32), kept)
+
+    def test_split_kv_helpers_need_a_process_group_only_for_the_exchange(self):
+        from tasft_b200 import shards as SH  # noqa: PLC0415
+
+        # the planning helpers are plain host/tensor code
+        assert SH.block_range(10, 0, 3) == (0, 4)
+        kept = KeptBlocks(torch.tensor([[[0, 5, 9]]], dtype=torch.int32), torch.tensor([[3]], dtype=torch.int32))
+        assert SH.local_kept(kept, 4, 10).idx.tolist() == [[[1, 5, -1]]]
