@@ -39,6 +39,35 @@ def default_splits(B: int, Hk: int, mean_kept: float, sms: int = 148) -> int:
     return max(1, min(fit, by_size, 16))
 
 
+def _decode_args(q, k, v, kv_len, kept: KeptBlocks, block, L_logical, Hk, num_splits, workspace, out, partials,
+                 err):
+    """The ``tasft_decode_args`` both decode entry points share (``k``/``v`` are the caches,
+    or the page pools for the paged call), with the split count and workspace resolved."""
+    B, Hq, D = q.shape
+    idx = kept.idx.contiguous()
+    cnt = kept.cnt.contiguous()
+    ws_ptr, ws_bytes = None, 0
+    if num_splits != 1:
+        if workspace is None:
+            ms = num_splits if num_splits > 0 else 16
+            workspace = DecodeWorkspace(B, Hq, Hk, D, ms, q.device)
+        ws_ptr, ws_bytes = workspace.buf.data_ptr(), workspace.bytes
+        if num_splits <= 0:
+            num_splits = min(workspace.max_splits, default_splits(B, Hk, idx.shape[-1] / 4))
+    args = L.DecodeArgs(
+        q=q.data_ptr(), k_cache=k.data_ptr(), v_cache=v.data_ptr(), out=L.ptr(out),
+        q_stride=L.strides3(q), k_stride=L.strides4(k), v_stride=L.strides4(v),
+        o_stride=L.strides3(out) if out is not None else L.I64x3(0, 0, 0),
+        B=B, Hq=Hq, Hk=Hk, L=L_logical, D=D, block=block, dtype=L.dtype_code(q), scale=1.0 / math.sqrt(D),
+        kv_len=kv_len.data_ptr(), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(), nb_max=idx.shape[-1],
+        num_splits=num_splits, part_o=L.ptr(partials[0]) if partials else None,
+        part_ml=L.ptr(partials[1]) if partials else None, workspace=ws_ptr, workspace_bytes=ws_bytes,
+        err=L.ptr(err),
+    )
+    # keep the tensors the struct points into alive until the call returns
+    return args, num_splits, (idx, cnt, workspace)
+
+
 def bsa_decode(
     q: torch.Tensor,
     k_cache: torch.Tensor,
@@ -68,28 +97,10 @@ def bsa_decode(
     q = q.contiguous()
     k_cache = k_cache.contiguous()
     v_cache = v_cache.contiguous()
-    idx = kept.idx.contiguous()
-    cnt = kept.cnt.contiguous()
     if out is None and partials is None:
         out = torch.empty_like(q)
-    ws_ptr, ws_bytes = None, 0
-    if num_splits != 1:
-        if workspace is None:
-            ms = num_splits if num_splits > 0 else 16
-            workspace = DecodeWorkspace(B, Hq, Hk, D, ms, q.device)
-        ws_ptr, ws_bytes = workspace.buf.data_ptr(), workspace.bytes
-        if num_splits <= 0:
-            num_splits = min(workspace.max_splits, default_splits(B, Hk, idx.shape[-1] / 4))
-    args = L.DecodeArgs(
-        q=q.data_ptr(), k_cache=k_cache.data_ptr(), v_cache=v_cache.data_ptr(), out=L.ptr(out),
-        q_stride=L.strides3(q), k_stride=L.strides4(k_cache), v_stride=L.strides4(v_cache),
-        o_stride=L.strides3(out) if out is not None else L.I64x3(0, 0, 0),
-        B=B, Hq=Hq, Hk=Hk, L=Lc, D=D, block=block, dtype=L.dtype_code(q), scale=1.0 / math.sqrt(D),
-        kv_len=kv_len.data_ptr(), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(), nb_max=idx.shape[-1],
-        num_splits=num_splits, part_o=L.ptr(partials[0]) if partials else None,
-        part_ml=L.ptr(partials[1]) if partials else None, workspace=ws_ptr, workspace_bytes=ws_bytes,
-        err=L.ptr(err),
-    )
+    args, num_splits, _keep = _decode_args(q, k_cache, v_cache, kv_len, kept, block, Lc, Hk, num_splits, workspace,
+                                           out, partials, err)
     L.check(L.lib().tasft_bsa_decode_fwd(args, L.stream_ptr(q.device)), "tasft_bsa_decode_fwd",
             shape=[B, Hq, Hk, Lc, D], splits=num_splits)
     return out
@@ -129,28 +140,10 @@ def bsa_decode_paged(
         raise KernelError("paged decode shape mismatch", context={"q": list(q.shape), "k": list(k_pages.shape)})
     q = q.contiguous()
     table = block_table.to(torch.int32).contiguous()
-    idx = kept.idx.contiguous()
-    cnt = kept.cnt.contiguous()
     if out is None and partials is None:
         out = torch.empty_like(q)
-    ws_ptr, ws_bytes = None, 0
-    if num_splits != 1:
-        if workspace is None:
-            ms = num_splits if num_splits > 0 else 16
-            workspace = DecodeWorkspace(B, Hq, Hk, D, ms, q.device)
-        ws_ptr, ws_bytes = workspace.buf.data_ptr(), workspace.bytes
-        if num_splits <= 0:
-            num_splits = min(workspace.max_splits, default_splits(B, Hk, idx.shape[-1] / 4))
-    base = L.DecodeArgs(
-        q=q.data_ptr(), k_cache=k_pages.data_ptr(), v_cache=v_pages.data_ptr(), out=L.ptr(out),
-        q_stride=L.strides3(q), k_stride=L.strides4(k_pages), v_stride=L.strides4(v_pages),
-        o_stride=L.strides3(out) if out is not None else L.I64x3(0, 0, 0),
-        B=B, Hq=Hq, Hk=Hk, L=max_pages * page_size, D=D, block=block, dtype=L.dtype_code(q),
-        scale=1.0 / math.sqrt(D), kv_len=kv_len.data_ptr(), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(),
-        nb_max=idx.shape[-1], num_splits=num_splits, part_o=L.ptr(partials[0]) if partials else None,
-        part_ml=L.ptr(partials[1]) if partials else None, workspace=ws_ptr, workspace_bytes=ws_bytes,
-        err=L.ptr(err),
-    )
+    base, num_splits, _keep = _decode_args(q, k_pages, v_pages, kv_len, kept, block, max_pages * page_size, Hk,
+                                           num_splits, workspace, out, partials, err)
     args = L.PagedDecodeArgs(base=base, block_table=table.data_ptr(), max_pages=max_pages, page_size=page_size,
                              num_pages=num_pages)
     L.check(L.lib().tasft_bsa_decode_paged_fwd(args, L.stream_ptr(q.device)), "tasft_bsa_decode_paged_fwd",
