@@ -5,7 +5,9 @@
  * Conventions
  *   - Every pointer in an args struct is a DEVICE pointer unless its comment says
  *     otherwise. The caller owns every buffer, including the workspace whose size
- *     the matching *_workspace_size() call returns. The library keeps no allocation.
+ *     the matching *_workspace_size() call returns. The library keeps no allocation,
+ *     with one exception: tasft_bsa_decode_fwd_noalloc's static per-device scratch
+ *     array of tasft_decode_noalloc_capacity() bytes.
  *   - Strides are in ELEMENTS (int64). Tensors are 4-D [batch, heads, seq, dim]
  *     unless stated; the innermost (dim) stride must be 1.
  *   - Launches are asynchronous on the given stream; no call synchronises the host.
@@ -25,6 +27,8 @@
  *   tasft_bsa_decode_combine   (none: split-KV (m,l,o) merge for multi-GPU decode)
  *   tasft_gate_target_fwd      TASFTAttention scores + compute_gate_target
  *                              tasft/modules/tasft_attention.py:427-458,
+ *                              tasft/training/objectives.py:128-185
+ *   tasft_gate_target_from_scores  compute_gate_target on a score tensor
  *                              tasft/training/objectives.py:128-185
  *   tasft_gate_loss_fwd_bwd    compute_gate_loss + compute_sparsity_loss (+ grad)
  *                              tasft/training/objectives.py:187-241
@@ -191,7 +195,7 @@ typedef struct {
   int32_t num_splits;     /* 0 = choose; else CTAs per (sequence, kv-head) */
   float* part_o;          /* optional out [B, Hq, D] fp32 normalised partial (for cross-GPU combine) */
   float* part_ml;         /* optional out [B, Hq, 2] fp32 (m, l) in base-e units */
-  void* workspace;        /* tasft_decode_workspace_size() bytes, zero-filled before first use */
+  void* workspace;        /* tasft_decode_workspace_size() bytes; the call clears its ticket prefix */
   int64_t workspace_bytes;
   int32_t* err;
 } tasft_decode_args;
@@ -203,7 +207,8 @@ TASFT_API int tasft_bsa_decode_fwd(const tasft_decode_args* args, tasft_stream_t
  * cudaMalloc). No counterpart in the reference. The split-KV scratch is a fixed
  * per-device array of tasft_decode_noalloc_capacity() bytes (4 MiB) inside the library;
  * args->workspace is ignored. The first call on a device looks the array up and should
- * come before any stream capture. All calls on a device share the array: calls that
+ * come before any stream capture. The address is cached per device for the life of the
+ * process; after cudaDeviceReset on that device the entry point must not be called again. All calls on a device share the array: calls that
  * overlap on the GPU race; order them on one stream. A call that needs more scratch than
  * the capacity returns TASFT_ERR_TOO_LARGE without launching. Nothing is allocated. */
 TASFT_API int tasft_bsa_decode_fwd_noalloc(const tasft_decode_args* args, tasft_stream_t stream);
@@ -264,6 +269,31 @@ typedef struct {
 } tasft_target_args;
 TASFT_API int64_t tasft_gate_target_workspace_size(int32_t B, int32_t Hq, int32_t S, int32_t block);
 TASFT_API int tasft_gate_target_fwd(const tasft_target_args* args, tasft_stream_t stream);
+
+/* Gate target from a score tensor the caller already holds, e.g. the pre-softmax
+ * attention scores [B, H, Sq, Sk] a training forward kept (-inf above the diagonal):
+ * -inf padding to whole blocks, block x block max-pool, optional clamp of finite maxima,
+ * softmax over the NBq*NBk grid divided by `temperature`. Replaces
+ * TASFTObjective.compute_gate_target (tasft/training/objectives.py:128-185; temperature 1,
+ * no clamp) and TASFTAttention._compute_gate_target (tasft/modules/tasft_attention.py:
+ * 220-290; temperature 2, clamp 50). Reads the whole tensor once (HBM-bound) and reports
+ * NaN (bit 0) and +inf (bit 1) in *flags, which the reference rejects. */
+typedef struct {
+  const void* scores;     /* [B, H, Sq, Sk] dtype */
+  int64_t stride[4];
+  int32_t B, H, Sq, Sk;
+  int32_t block;          /* 1..1024 */
+  int32_t dtype;
+  float temperature;      /* softmax divides the maxima by this (<= 0: 1) */
+  float clamp;            /* <= 0: none; else clamp finite maxima to [-clamp, clamp] */
+  float* block_max;       /* out [B, H, NBq, NBk] fp32, or NULL (then the workspace holds it) */
+  float* target;          /* out [B, H, NBq, NBk] fp32 */
+  int32_t* flags;         /* optional device word, OR-ed: 1 = NaN seen, 2 = +inf seen */
+  void* workspace;        /* tasft_scores_target_workspace_size() bytes when block_max is NULL */
+  int64_t workspace_bytes;
+} tasft_scores_target_args;
+TASFT_API int64_t tasft_scores_target_workspace_size(int32_t B, int32_t H, int32_t Sq, int32_t Sk, int32_t block);
+TASFT_API int tasft_gate_target_from_scores(const tasft_scores_target_args* args, tasft_stream_t stream);
 
 typedef struct {
   const float* soft;      /* [B, H, NB, NB] gate scores */

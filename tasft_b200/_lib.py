@@ -107,6 +107,15 @@ class TargetArgs(C.Structure):
     ]
 
 
+class ScoresTargetArgs(C.Structure):
+    _fields_ = [
+        ("scores", vp), ("stride", I64x4), ("B", C.c_int32), ("H", C.c_int32), ("Sq", C.c_int32),
+        ("Sk", C.c_int32), ("block", C.c_int32), ("dtype", C.c_int32), ("temperature", C.c_float),
+        ("clamp", C.c_float), ("block_max", vp), ("target", vp), ("flags", vp), ("workspace", vp),
+        ("workspace_bytes", C.c_int64),
+    ]
+
+
 class LossArgs(C.Structure):
     _fields_ = [
         ("soft", vp), ("target", vp), ("B", C.c_int32), ("H", C.c_int32), ("NBq", C.c_int32), ("NBk", C.c_int32),
@@ -142,6 +151,8 @@ SIGNATURES = {
     "tasft_decode_noalloc_capacity": ([], C.c_int64),
     "tasft_gate_target_workspace_size": ([C.c_int32] * 4, C.c_int64),
     "tasft_gate_target_fwd": ([C.POINTER(TargetArgs), vp], C.c_int),
+    "tasft_scores_target_workspace_size": ([C.c_int32] * 5, C.c_int64),
+    "tasft_gate_target_from_scores": ([C.POINTER(ScoresTargetArgs), vp], C.c_int),
     "tasft_gate_loss_workspace_size": ([C.c_int32] * 2, C.c_int64),
     "tasft_gate_loss_fwd_bwd": ([C.POINTER(LossArgs), vp], C.c_int),
     "tasft_gate_bwd_workspace_size": ([C.c_int32] * 6, C.c_int64),

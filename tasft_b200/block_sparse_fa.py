@@ -8,9 +8,12 @@ additive or stricter:
 * K/V may have fewer heads than Q (GQA, ``Hq % Hk == 0``); no ``repeat_interleave``.
 * ``block_mask`` may be a bool ``[B, Hm, NB, NB]`` mask with ``Hm`` = q-heads or
   kv-heads, or a precomputed :class:`~tasft_b200.types.KeptBlocks`.
-* There is one backend (the CUDA library) and no dense fallback: a call below
+* There is one compute backend (the CUDA library). Under ``AUTO`` a call below
   ``min_sparsity_for_speedup`` still runs the sparse kernel on the given mask (the
-  reference would run dense SDPA and ignore the mask, :393-399). No host sync.
+  reference would run dense SDPA and ignore the mask, :393-399), with no host sync. An
+  explicit ``DENSE_FALLBACK`` backend is accepted as the reference accepts it
+  (:340-359) and, like the reference's dense path, ignores the mask: it runs full
+  (causal) attention through the same kernel with every block kept.
 """
 from __future__ import annotations
 
@@ -39,12 +42,36 @@ class KernelBackend(Enum):
 
 
 def detect_kernels() -> list[KernelBackend]:
-    """Available backends: the sm_100a CUDA library when it loads, else none."""
+    """Available backends in priority order; ``DENSE_FALLBACK`` is always the last element
+    (the reference's guarantee, block_sparse_fa.py:63-90). ``SM100_CUDA`` is listed when
+    the sm_100a library loads. Both run on that library: without it the constructor
+    raises, there is no CPU path."""
     try:
         L.lib()
     except KernelError:
-        return []
-    return [KernelBackend.SM100_CUDA]
+        return [KernelBackend.DENSE_FALLBACK]
+    return [KernelBackend.SM100_CUDA, KernelBackend.DENSE_FALLBACK]
+
+
+_FULL_LISTS: dict = {}
+
+
+def full_kept(B: int, H: int, nb: int, causal: bool, device) -> KeptBlocks:
+    """Kept lists with every block (of the lower triangle when causal): dense attention
+    through the block-sparse kernel. Cached per shape and device."""
+    key = (B, H, nb, causal, str(device))
+    kb = _FULL_LISTS.get(key)
+    if kb is None:
+        ar = torch.arange(nb, dtype=torch.int32, device=device)
+        idx = ar.view(1, nb).expand(nb, nb).clone()
+        if causal:
+            idx = torch.where(ar.view(nb, 1) >= ar.view(1, nb), idx, torch.full_like(idx, -1))
+            cnt = ar + 1
+        else:
+            cnt = torch.full((nb,), nb, dtype=torch.int32, device=device)
+        kb = KeptBlocks(idx.expand(B, H, nb, nb).contiguous(), cnt.expand(B, H, nb).contiguous())
+        _FULL_LISTS[key] = kb
+    return kb
 
 
 @dataclass(frozen=True, slots=True)
@@ -86,7 +113,9 @@ class BlockSparseFlashAttention:
     Args:
         block_size: 32, 64 or 128 (64 runs on the tcgen05 tensor-core kernel for bf16/fp16).
         min_sparsity_for_speedup: validated and kept for API compatibility.
-        backend: ``AUTO`` or ``SM100_CUDA``; any other value raises ``KernelError``.
+        backend: ``AUTO`` / ``SM100_CUDA`` (block-sparse), or ``DENSE_FALLBACK`` (full
+            attention, mask ignored, as the reference's dense backend); the reference's
+            ``TRITON`` and ``FLASH_ATTN_SPARSE`` raise ``KernelError``.
     """
 
     def __init__(
@@ -102,13 +131,15 @@ class BlockSparseFlashAttention:
         self.block_size = block_size
         self.min_sparsity_for_speedup = min_sparsity_for_speedup
         self._available_backends = detect_kernels()
-        if backend not in (KernelBackend.AUTO, KernelBackend.SM100_CUDA) or not self._available_backends:
+        if backend not in self._available_backends + [KernelBackend.AUTO] or \
+                KernelBackend.SM100_CUDA not in self._available_backends:
             names = [b.name for b in self._available_backends]
             raise KernelError(
                 f"Requested backend {backend.name} is not available. Available: {names}",
                 context={"requested": backend.name, "available": names},
             )
-        self.backend = KernelBackend.SM100_CUDA
+        self.backend = KernelBackend.DENSE_FALLBACK if backend == KernelBackend.DENSE_FALLBACK \
+            else KernelBackend.SM100_CUDA
         self.force_simt = False  # testing hook: run the CUDA-core kernel instead of tcgen05
 
     # ------------------------------------------------------------------
@@ -130,7 +161,10 @@ class BlockSparseFlashAttention:
         q = q.contiguous()
         k = k.contiguous()
         v = v.contiguous()
-        kept = block_mask if isinstance(block_mask, KeptBlocks) else mask_to_kept(block_mask, causal)
+        if self.backend == KernelBackend.DENSE_FALLBACK:
+            kept = full_kept(B, Hk, math.ceil(S / self.block_size), causal, q.device)
+        else:
+            kept = block_mask if isinstance(block_mask, KeptBlocks) else mask_to_kept(block_mask, causal)
         if out is None:
             out = torch.empty_like(q)
         idx = kept.idx.contiguous()
@@ -247,4 +281,4 @@ class BlockSparseFlashAttention:
         return 1.0 / max(1e-6, 1.0 - sparsity_ratio * (1.0 - 0.02))
 
 
-__all__ = ["BlockSparseFlashAttention", "KernelBackend", "SparsityStats", "detect_kernels", "mask_to_kept"]
+__all__ = ["BlockSparseFlashAttention", "KernelBackend", "SparsityStats", "detect_kernels", "full_kept", "mask_to_kept"]

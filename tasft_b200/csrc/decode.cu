@@ -327,9 +327,15 @@ extern "C" int64_t tasft_decode_workspace_size(int32_t B, int32_t Hq, int32_t Hk
   return tick + (part + 255) / 256 * 256;
 }
 
+namespace tasft {
+int decode_check_args(const tasft_decode_args& a);
+int decode_pick_splits(const tasft_decode_args& a);
+int decode_run(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st);
+}  // namespace tasft
+
 // Workspace layout: [tickets: B*Hk int32 + 2 work counters, padded to 256 B][partials: B*Hq x nsplit x (D+2) fp32].
-// Tickets sit first so their place does not depend on the split count; every call
-// leaves them at zero again.
+// Tickets sit first so their place does not depend on the split count; every split call
+// clears them before its launch.
 static int decode_ws_from(const tasft_decode_args& a, int nsplit, DecodeWs* ws) {
   const int64_t tick = ((int64_t)(a.B * a.Hk + 2) * 4 + 255) / 256 * 256;
   const int64_t need = tick + (int64_t)a.B * a.Hq * nsplit * (a.D + 2) * 4;
@@ -340,49 +346,30 @@ static int decode_ws_from(const tasft_decode_args& a, int nsplit, DecodeWs* ws) 
   return TASFT_OK;
 }
 
+// Tickets and work counters are cleared on the caller's stream at the start of every
+// split call, so a call that follows one whose bounded wait gave up (and therefore left
+// its tickets behind) starts from a clean state.
+static int decode_clear_tickets(const tasft_decode_args& a, const DecodeWs& ws, cudaStream_t st) {
+  const size_t tick = (size_t)(a.B * a.Hk + 2) * 4;
+  return cudaMemsetAsync(ws.ticket, 0, tick, st) == cudaSuccess ? TASFT_OK : TASFT_ERR_CUDA;
+}
+
 extern "C" int tasft_bsa_decode_fwd(const tasft_decode_args* ap, tasft_stream_t stream) {
   if (!ap) return TASFT_ERR_INVALID_ARG;
   const tasft_decode_args& a = *ap;
-  if (!a.q || !a.k_cache || !a.v_cache || !a.kv_len || !a.kept_idx || !a.kept_cnt) return TASFT_ERR_INVALID_ARG;
-  if (!a.out && !a.part_o) return TASFT_ERR_INVALID_ARG;
-  if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.L <= 0 || a.block <= 0 || a.nb_max <= 0) return TASFT_ERR_INVALID_ARG;
-  if (a.Hq % a.Hk != 0 || a.Hq / a.Hk > kGmax) return TASFT_ERR_UNSUPPORTED;
-  if (a.block > 128 || a.block % 8 != 0) return TASFT_ERR_UNSUPPORTED;
-  const int es = elem_size(a.dtype);
-  // bulk copies need contiguous 16-byte aligned rows
-  if (a.k_stride[3] != 1 || a.v_stride[3] != 1 || a.k_stride[2] != a.D || a.v_stride[2] != a.D ||
-      a.q_stride[2] != 1 || (a.out && a.o_stride[2] != 1))
-    return TASFT_ERR_INVALID_ARG;
-  if (!aligned16(a.k_cache) || !aligned16(a.v_cache) || !aligned16(a.q) || (a.k_stride[1] * es) % 16 ||
-      (a.v_stride[1] * es) % 16 || (a.k_stride[0] * es) % 16 || (a.v_stride[0] * es) % 16 ||
-      (a.q_stride[1] * es) % 16 || (a.q_stride[0] * es) % 16)
-    return TASFT_ERR_INVALID_ARG;
-  int nsplit = a.num_splits;
-  if (nsplit <= 0) {
-    const int units = a.B * a.Hk;
-    nsplit = (6 * 148) / units;  // items within the resident CTA slots
-    int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
-    if (cap > 16) cap = 16;  // the last split merges all partials with one warp
-    if (nsplit > cap) nsplit = cap;
-    if (nsplit < 1) nsplit = 1;
-  }
+  int rc = decode_check_args(a);
+  if (rc != TASFT_OK) return rc;
+  const int nsplit = decode_pick_splits(a);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   DecodeWs ws{nullptr, nullptr, 0};
   if (nsplit > 1) {
     if (!a.workspace) return TASFT_ERR_WORKSPACE;
-    const int rc = decode_ws_from(a, nsplit, &ws);
+    rc = decode_ws_from(a, nsplit, &ws);
+    if (rc != TASFT_OK) return rc;
+    rc = decode_clear_tickets(a, ws, st);
     if (rc != TASFT_OK) return rc;
   }
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (a.dtype != TASFT_F32) {
-    const int rc = decode_mma(a, ws, nsplit, st);
-    if (rc != TASFT_ERR_UNSUPPORTED) return rc;
-  }
-  switch (a.dtype) {
-    case TASFT_F32: return launch_decode_dt<float>(a, ws, nsplit, st);
-    case TASFT_BF16: return launch_decode_dt<__nv_bfloat16>(a, ws, nsplit, st);
-    case TASFT_F16: return launch_decode_dt<__half>(a, ws, nsplit, st);
-    default: return TASFT_ERR_UNSUPPORTED;
-  }
+  return decode_run(a, ws, nsplit, st);
 }
 
 extern "C" int tasft_bsa_decode_combine(const tasft_combine_args* ap, tasft_stream_t stream) {
@@ -401,8 +388,8 @@ extern "C" int tasft_bsa_decode_combine(const tasft_combine_args* ap, tasft_stre
 }
 
 // ---------------------------------------------------------------------------
-// Helpers for entry points that bring their own scratch (decode_noalloc.cu). They
-// repeat the argument checks, split choice and kernel dispatch of tasft_bsa_decode_fwd.
+// Argument checks, split choice and kernel dispatch, shared by tasft_bsa_decode_fwd and
+// the entry point that brings its own scratch (decode_noalloc.cu).
 // ---------------------------------------------------------------------------
 namespace tasft {
 
@@ -476,7 +463,9 @@ extern "C" int tasft_bsa_decode_paged_fwd(const tasft_paged_decode_args* pp, tas
   DecodeWs ws{nullptr, nullptr, 0};
   if (nsplit > 1) {
     if (!a.workspace) return TASFT_ERR_WORKSPACE;
-    const int rc = decode_ws_from(a, nsplit, &ws);
+    int rc = decode_ws_from(a, nsplit, &ws);
+    if (rc != TASFT_OK) return rc;
+    rc = decode_clear_tickets(a, ws, reinterpret_cast<cudaStream_t>(stream));
     if (rc != TASFT_OK) return rc;
   }
   return decode_mma_paged(a, ws, nsplit, pp->block_table, pp->max_pages, ps, pp->num_pages,

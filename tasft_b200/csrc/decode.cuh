@@ -9,7 +9,7 @@ namespace tasft {
 
 struct DecodeWs {
   float* part;      // [B*Hq, nsplit, D + 2]  (normalised o, m (base e), l)
-  int32_t* ticket;  // [B*Hk], zero between calls
+  int32_t* ticket;  // [B*Hk] + 2 work counters, cleared by the host before each split call
   int max_splits;
 };
 

@@ -65,6 +65,80 @@ __global__ void __launch_bounds__(256) blockmax_simt_kernel(tasft_target_args a,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Block max of a given score tensor (objectives.py:128-185: -inf padding, 2-D max-pool
+// over block x block tiles). HBM-bound streaming read: one CTA per (b*h, q-block,
+// window of kpc k-blocks); warp w reads rows w, w+8, ... of the q-block, each thread a
+// VEC-wide (16-byte when aligned) column slice, so a warp row load is 32 x 16 B
+// contiguous. Per-warp column maxima meet in shared memory, then one warp per k-block
+// reduces its columns. NaN and +inf are flagged (the reference raises on them).
+// ---------------------------------------------------------------------------
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) scores_blockmax_kernel(tasft_scores_target_args a, float* bm, int NBq,
+                                                              int NBk, int kpc) {
+  extern __shared__ float colmax[];  // [8][W]
+  const int W = kpc * a.block;
+  const int kb0 = blockIdx.x * kpc;
+  const int qb = blockIdx.y;
+  const int bh = blockIdx.z;
+  const int b = bh / a.H, h = bh % a.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* base = reinterpret_cast<const T*>(a.scores) + b * a.stride[0] + h * a.stride[1];
+  const int r0 = qb * a.block;
+  const int rows = min(a.block, a.Sq - r0);
+  const int c0 = kb0 * a.block;
+  bool bad_nan = false, bad_inf = false;
+  for (int cc = lane * VEC; cc < W; cc += 32 * VEC) {
+    float m[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) m[j] = -INFINITY;
+    const int col = c0 + cc;
+    if (col < a.Sk) {
+      const T* p = base + (int64_t)col * a.stride[3];
+#pragma unroll 4
+      for (int r = warp; r < rows; r += 8) {
+        const T* pr = p + (int64_t)(r0 + r) * a.stride[2];
+        if (VEC > 1) {
+          // VEC > 1 only when Sk % VEC == 0 and the rows are 16-byte aligned
+          uint4 raw = __ldcs(reinterpret_cast<const uint4*>(pr));
+          const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            const float x = to_f<T>(e[j]);
+            bad_nan |= x != x;
+            bad_inf |= x == INFINITY;
+            m[j] = fmaxf(m[j], x);
+          }
+        } else {
+          const float x = to_f<T>(pr[0]);
+          bad_nan |= x != x;
+          bad_inf |= x == INFINITY;
+          m[0] = fmaxf(m[0], x);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) colmax[warp * W + cc + j] = m[j];
+  }
+  __syncthreads();
+  for (int kl = warp; kl < kpc; kl += 8) {
+    const int kb = kb0 + kl;
+    if (kb >= NBk) break;
+    float mx = -INFINITY;
+    for (int c = lane; c < a.block; c += 32) {
+      const int cc = kl * a.block + c;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) mx = fmaxf(mx, colmax[w * W + cc]);
+    }
+    mx = warp_max(mx);
+    if (lane == 0) bm[((int64_t)bh * NBq + qb) * NBk + kb] = mx;
+  }
+  if (a.flags) {
+    const unsigned any_nan = __ballot_sync(0xffffffffu, bad_nan), any_inf = __ballot_sync(0xffffffffu, bad_inf);
+    if (lane == 0 && (any_nan | any_inf)) atomicOr(a.flags, (any_nan ? 1 : 0) | (any_inf ? 2 : 0));
+  }
+}
+
 // Softmax over each (b, h) grid of NB*NB block maxima (objectives.py:180-185), with the
 // alternate target's clamp and temperature (tasft_attention.py:278-289) as options.
 __global__ void target_softmax_kernel(const float* bm, float* target, int64_t n, float inv_temp, float clamp) {
@@ -367,6 +441,63 @@ extern "C" int tasft_gate_target_fwd(const tasft_target_args* ap, tasft_stream_t
   if (rc != TASFT_OK) return rc;
   const float inv_t = a.temperature > 0.f ? 1.0f / a.temperature : 1.0f;
   target_softmax_kernel<<<a.B * a.Hq, 512, 0, st>>>(bm, a.target, (int64_t)NB * NB, inv_t, a.clamp);
+  count_launch();
+  return launch_status();
+}
+
+template <typename T, int VEC>
+static int launch_scores_bm(const tasft_scores_target_args& a, float* bm, int NBq, int NBk, cudaStream_t st) {
+  const int kpc = a.block >= 256 ? 1 : 256 / a.block;
+  const size_t smem = (size_t)8 * kpc * a.block * sizeof(float);
+  auto kern = scores_blockmax_kernel<T, VEC>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return TASFT_ERR_CUDA;
+  dim3 grid((unsigned)ceil_div(NBk, kpc), (unsigned)NBq, (unsigned)(a.B * a.H));
+  kern<<<grid, 256, smem, st>>>(a, bm, NBq, NBk, kpc);
+  count_launch();
+  return launch_status();
+}
+
+template <typename T>
+static int launch_scores_bm_dt(const tasft_scores_target_args& a, float* bm, int NBq, int NBk, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const bool vec = a.stride[3] == 1 && a.block % V == 0 && a.Sk % V == 0 && aligned16(a.scores) &&
+                   (a.stride[2] * (int64_t)sizeof(T)) % 16 == 0 && (a.stride[1] * (int64_t)sizeof(T)) % 16 == 0 &&
+                   (a.stride[0] * (int64_t)sizeof(T)) % 16 == 0;
+  return vec ? launch_scores_bm<T, V>(a, bm, NBq, NBk, st) : launch_scores_bm<T, 1>(a, bm, NBq, NBk, st);
+}
+
+extern "C" int64_t tasft_scores_target_workspace_size(int32_t B, int32_t H, int32_t Sq, int32_t Sk, int32_t block) {
+  if (B <= 0 || H <= 0 || Sq <= 0 || Sk <= 0 || block <= 0) return -1;
+  return ((int64_t)B * H * ceil_div(Sq, block) * ceil_div(Sk, block) * 4 + 255) / 256 * 256;
+}
+
+extern "C" int tasft_gate_target_from_scores(const tasft_scores_target_args* ap, tasft_stream_t stream) {
+  if (!ap) return TASFT_ERR_INVALID_ARG;
+  const tasft_scores_target_args& a = *ap;
+  if (!a.scores || !a.target || a.B <= 0 || a.H <= 0 || a.Sq <= 0 || a.Sk <= 0 || a.block <= 0)
+    return TASFT_ERR_INVALID_ARG;
+  if (a.block > 1024) return TASFT_ERR_UNSUPPORTED;
+  const int NBq = ceil_div(a.Sq, a.block), NBk = ceil_div(a.Sk, a.block);
+  if ((int64_t)a.B * a.H > 65535 || NBq > 65535) return TASFT_ERR_UNSUPPORTED;
+  float* bm = a.block_max;
+  if (!bm) {
+    if (!a.workspace || a.workspace_bytes < tasft_scores_target_workspace_size(a.B, a.H, a.Sq, a.Sk, a.block))
+      return TASFT_ERR_WORKSPACE;
+    bm = reinterpret_cast<float*>(a.workspace);
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc;
+  switch (a.dtype) {
+    case TASFT_F32: rc = launch_scores_bm_dt<float>(a, bm, NBq, NBk, st); break;
+    case TASFT_BF16: rc = launch_scores_bm_dt<__nv_bfloat16>(a, bm, NBq, NBk, st); break;
+    case TASFT_F16: rc = launch_scores_bm_dt<__half>(a, bm, NBq, NBk, st); break;
+    default: return TASFT_ERR_UNSUPPORTED;
+  }
+  if (rc != TASFT_OK) return rc;
+  const float inv_t = a.temperature > 0.f ? 1.0f / a.temperature : 1.0f;
+  target_softmax_kernel<<<a.B * a.H, 512, 0, st>>>(bm, a.target, (int64_t)NBq * NBk, inv_t, a.clamp);
   count_launch();
   return launch_status();
 }

@@ -123,7 +123,9 @@ def _objective_cases(obj):
 
 
 def main() -> None:
-    root = Path(os.environ.get("TASFT_REFERENCE", "/root/reference"))
+    if "TASFT_REFERENCE" not in os.environ:
+        raise SystemExit("set TASFT_REFERENCE to the reference checkout (the folder holding tasft/)")
+    root = Path(os.environ["TASFT_REFERENCE"])
     attn_gate, bsfa, obj = _load_reference(root)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     data = {

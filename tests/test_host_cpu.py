@@ -10,6 +10,7 @@ import pytest
 import torch
 
 import oracle as O
+from conftest import import_reference
 from tasft_b200 import AttnGate, BlockSparseFlashAttention, KernelBackend, KernelError, KeptBlocks, ValidationError
 from tasft_b200 import masks as M
 
@@ -75,10 +76,7 @@ class TestAttnGateHost:
             AttnGate(**kw)
 
     def test_state_dict_compatible_with_reference(self):
-        ref_root = Path("/root/reference")
-        if not ref_root.exists():
-            pytest.skip("reference checkout not present")
-        sys.path.insert(0, str(ref_root))
+        import_reference()
         from tasft.modules.attn_gate import AttnGate as RefGate  # noqa: PLC0415
         ref = RefGate(4, 64, block_size=64)
         ours = AttnGate(4, 64, block_size=64)
@@ -152,10 +150,7 @@ class TestMaskRules:
 
 
 def test_patch_into_reference():
-    ref_root = Path("/root/reference")
-    if not ref_root.exists():
-        pytest.skip("reference checkout not present")
-    sys.path.insert(0, str(ref_root))
+    import_reference()
     import tasft_b200
 
     names = tasft_b200.patch()
