@@ -276,6 +276,266 @@ def cpu_prefill_sample(budget_s: float = 10.0):
                       f"(oracle/tasft_oracle.py:bsa_prefill_masked_dense), {dt:.1f} s"}
 
 
+# ---------------------------------------------------------------------------
+def bench_dropin(q, k, v, gate, kern, flush, ws, args, peaks):
+    """Prefill in the form the reference callers use (tasft_attention.py:574-593, 725-729):
+    K/V repeated per q-head (Hk = Hq) and the gate's per-q-head masks. Also the reference's
+    own Triton kernel (block_sparse_fa.py:108-269) on the same inputs when the reference
+    package is importable (baseline/_ref), on one GPU only."""
+    import tasft_b200 as T  # noqa: PLC0415
+    from tasft_b200 import masks as M  # noqa: PLC0415
+
+    grp = CFG["Hq"] // CFG["Hk"]
+    ke = k.repeat_interleave(grp, dim=1)
+    ve = v.repeat_interleave(grp, dim=1)
+    with torch.no_grad():
+        sc = gate(q, ke).soft_scores  # per q-head fp32 scores over the expanded K
+    mask_q = M.prefill_mask(sc, CFG["density"])  # [B, Hq, NB, NB]
+    kept_q = T.mask_to_kept(mask_q, True)
+    kept_blocks = int(mask_q.sum().item())
+    flops = kept_blocks * 4 * CFG["block"] * CFG["block"] * CFG["D"]
+    out = torch.empty_like(q)
+    t_k = time_steps(lambda: kern.forward(q, ke, ve, kept_q, out=out), args.steps, args.warmup, flush, ws)
+    t_f = time_steps(lambda: kern.forward(q, ke, ve, mask_q, out=out), args.steps, args.warmup, flush, ws)
+    ms_k, ms_f = statistics.mean(t_k), statistics.mean(t_f)
+    info = {"config": "BASELINE configs[1] as the reference callers pass it: K/V repeated to 32 heads, per-q-head "
+                      "gate masks (prefill_mask at density 0.2 on each q-head's scores)",
+            "kept_blocks": kept_blocks, "gflop": round(flops / 1e9, 3),
+            "ms_kernel": round(ms_k, 4), "ms_forward": round(ms_f, 4),
+            "tflops": round(flops / (ms_k * 1e-3) / 1e12, 2),
+            "frac": round(flops / (ms_k * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
+    if ws == 1 and not args.no_triton:
+        info["triton_ref"] = bench_triton_ref(q, ke, ve, mask_q, out, flops, ms_k, flush, args)
+    del ke, ve
+    return info
+
+
+def bench_triton_ref(q, ke, ve, mask_q, ours_out, flops, ours_ms, flush, args):
+    """The reference's Triton kernel JIT-compiled on this GPU, unmodified, through its own
+    ``_triton_forward`` (launch incl. its host-side mask prep) and ``forward`` (adds the
+    sparsity-stats host sync)."""
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "tasft" / "__init__.py").exists():
+        return {"unavailable": "reference package not installed in baseline/_ref"}
+    try:
+        if str(ref_root) not in sys.path:
+            sys.path.insert(0, str(ref_root))
+        from tasft.kernels.block_sparse_fa import BlockSparseFlashAttention as RefBSFA  # noqa: PLC0415
+        from tasft.kernels.block_sparse_fa import KernelBackend as RefBackend  # noqa: PLC0415
+
+        ref = RefBSFA(block_size=CFG["block"], backend=RefBackend.TRITON)
+        o_ref = ref._triton_forward(q, ke, ve, mask_q, True)  # JIT compile
+        torch.cuda.synchronize()
+        err = (o_ref.float() - ours_out.float()).abs().max().item()
+        steps = max(3, min(args.steps, 5))
+        t_l = time_steps(lambda: ref._triton_forward(q, ke, ve, mask_q, True), steps, 3, flush, 1)
+        t_f = time_steps(lambda: ref.forward(q, ke, ve, mask_q, causal=True), steps, 3, flush, 1)
+        ms_l, ms_f = statistics.mean(t_l), statistics.mean(t_f)
+        return {"ms_launch": round(ms_l, 4), "ms_forward": round(ms_f, 4),
+                "tflops": round(flops / (ms_l * 1e-3) / 1e12, 2),
+                "speedup_ours_vs_triton": round(ms_l / ours_ms, 2),
+                "max_abs_diff_vs_ours": round(err, 5),
+                "what": "unmodified reference _block_sparse_attn_fwd_kernel (Triton JIT on this B200) on the same "
+                        "expanded K/V and per-q-head masks"}
+    except Exception as e:  # noqa: BLE001 - record why the reference kernel did not run
+        return {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+
+
+def bench_gate_train(q, k, flush, ws, args):
+    """BASELINE configs[4] end to end: gate forward (autograd), target from Q and K, KL +
+    sparsity loss, backward to the gate parameters. Times the whole step and the
+    loss + backward part alone."""
+    import tasft_b200 as T  # noqa: PLC0415
+
+    torch.manual_seed(0)
+    gate = T.AttnGate(CFG["Hq"], CFG["D"], block_size=CFG["block"]).to(q.device)
+
+    def train_step():
+        go = gate(q, k)
+        tgt = T.gate_target_from_qk(q, k, CFG["block"])
+        total, _, _ = T.gate_objective(go.soft_scores, tgt, 0.8, 1.0, 0.01)
+        total.backward()
+
+    t_all = time_steps(train_step, args.steps, args.warmup, flush, ws)
+    st = torch.cuda.current_stream()
+    bw = []
+    for i in range(args.warmup + args.steps):
+        go = gate(q, k)
+        tgt = T.gate_target_from_qk(q, k, CFG["block"])
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        total, _, _ = T.gate_objective(go.soft_scores, tgt, 0.8, 1.0, 0.01)
+        total.backward()
+        e1.record(st)
+        if i >= args.warmup:
+            bw.append((e0, e1))
+    torch.cuda.synchronize()
+    ms_bw = statistics.mean(a.elapsed_time(b) for a, b in bw)
+    return {"config": "BASELINE configs[4]: B=4, Hq=32, Hk=8, S=4096, D=128, gate hidden 32; NB=64",
+            "ms_train_step": round(statistics.mean(t_all), 4), "ms_loss_and_backward": round(ms_bw, 4),
+            "kernels": "gate mask build + target_tc + target_softmax + loss_rows/final/add + gate bwd (5 kernels)",
+            "what": "AttnGate.forward (autograd) -> gate_target_from_qk -> gate_objective -> backward to "
+                    "gate_proj_in/out"}
+
+
+def bench_qwen_prefill(rank, ws, dev, flush, args, peaks):
+    """BASELINE configs[3] prefill: B=1, Hq=28, Hk=4, S=32768, 90% block sparsity. With N
+    ranks the q-blocks are cut into N ranges of equal kept work (``shards.qblock_ranges``);
+    each rank computes its range (strong scaling, no exchange)."""
+    import tasft_b200 as T  # noqa: PLC0415
+    from tasft_b200 import masks as M  # noqa: PLC0415
+    from tasft_b200 import shards as SH  # noqa: PLC0415
+
+    c = dict(B=1, Hq=28, Hk=4, S=32768, D=128, block=64, density=0.1)
+    g = torch.Generator(device=dev).manual_seed(4321)  # same inputs on every rank
+    q = torch.randn(c["B"], c["Hq"], c["S"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(c["B"], c["Hk"], c["S"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(c["B"], c["Hk"], c["S"], c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    torch.manual_seed(0)
+    gate = T.AttnGate(c["Hq"], c["D"], block_size=c["block"]).to(dev)
+    with torch.no_grad():
+        sc = M.group_max(gate(q, k).soft_scores, c["Hk"])
+    mask = M.prefill_mask(sc, c["density"])
+    kept = T.mask_to_kept(mask, True)
+    grp = c["Hq"] // c["Hk"]
+    total_blocks = int(mask.sum().item())
+    lo, hi = SH.qblock_ranges(kept, ws)[rank]
+    mine = SH.restrict_qblocks(kept, lo, hi) if ws > 1 else kept
+    my_blocks = int(mine.cnt.sum().item())
+    kern = T.BlockSparseFlashAttention(block_size=c["block"])
+    out = torch.empty_like(q)
+    t = time_steps(lambda: kern.forward(q, k, v, mine, out=out), args.steps, args.warmup, flush, ws)
+    ms = statistics.mean(t)
+    ms_max = max_over_ranks(ms, ws)
+    unit = grp * 4 * c["block"] * c["block"] * c["D"]
+    flops = total_blocks * unit
+    info = {"config": "BASELINE configs[3] prefill: B=1, Hq=28, Hk=4, S=32768, D=128, block 64, causal, 90% block "
+                      "sparsity (kv-head masks from the random-init gate)",
+            "gflop": round(flops / 1e9, 2), "ms": round(ms_max, 4),
+            "tflops": round(flops / (ms_max * 1e-3) / 1e12, 2),
+            "frac": round(flops / (ms_max * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+            "split": f"q-block ranges of equal kept work over {ws} rank(s)" if ws > 1 else "one GPU",
+            "scaling": "strong"}
+    if ws > 1:
+        info["rank_blocks_max_over_mean"] = round(max_over_ranks(float(my_blocks), ws) / (total_blocks / ws), 4)
+    del q, k, v, out
+    return info
+
+
+def bench_strong_c2(q, k, v, mask, rank, ws, flush, args, peaks):
+    """BASELINE configs[1] as ONE global B=4 layer split over the ranks by (sequence,
+    kv-head) units, balanced by kept blocks (``shards.assign_units``): strong scaling."""
+    import tasft_b200 as T  # noqa: PLC0415
+    from tasft_b200 import shards as SH  # noqa: PLC0415
+
+    kept = T.mask_to_kept(mask, True)
+    w = SH.unit_weights(kept, CFG["Hk"])
+    units = SH.assign_units(w, ws)[rank]
+    qu, ku, vu, ku_kept = SH.unit_slices(q, k, v, kept, units)
+    kern = T.BlockSparseFlashAttention(block_size=CFG["block"])
+    out = torch.empty_like(qu)
+    t = time_steps(lambda: kern.forward(qu, ku, vu, ku_kept, out=out), args.steps, args.warmup, flush, ws)
+    ms_max = max_over_ranks(statistics.mean(t), ws)
+    grp = CFG["Hq"] // CFG["Hk"]
+    total_blocks = int(w.sum().item())
+    flops = total_blocks * grp * 4 * CFG["block"] * CFG["block"] * CFG["D"]
+    mine = float(sum(int(w[u]) for u in units))
+    return {"config": "BASELINE configs[1], one global B=4 layer (32 sequence x kv-head units) split over the ranks",
+            "units_per_rank": len(units), "ms": round(ms_max, 4),
+            "tflops": round(flops / (ms_max * 1e-3) / 1e12, 2),
+            "frac_of_one_gpu_peak_x_n": round(flops / (ms_max * 1e-3) / 1e12 / (peaks["bf16_tflops"] * ws), 4),
+            "rank_blocks_max_over_mean": round(max_over_ranks(mine, ws) / (total_blocks / ws), 4),
+            "scaling": "strong"}
+
+
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(budget_s: float = 3.0):
+    """Oracle decode (restated single-query masked attention) on host cores: a few
+    sequences of the configs[2] workload."""
+    import oracle as O  # noqa: PLC0415  (CPU baseline leg)
+    from tasft_b200 import masks as M  # noqa: PLC0415
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = DEC
+    nseq = 2
+    g = torch.Generator().manual_seed(77)
+    q = torch.randn(nseq, c["Hq"], c["D"], generator=g).bfloat16()
+    kc = torch.randn(nseq, c["Hk"], c["L"], c["D"], generator=g).bfloat16()
+    vc = torch.randn(nseq, c["Hk"], c["L"], c["D"], generator=g).bfloat16()
+    kv_len = torch.full((nseq,), c["L"], dtype=torch.int32)
+    nb = c["L"] // c["block"]
+    idx, cnt = M.lists_from_mask(M.decode_mask(torch.rand(nseq, c["Hk"], nb, generator=g), kv_len // 64,
+                                               c["density"], nb))
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        O.bsa_decode(q, kc, vc, kv_len, idx, cnt, c["block"])
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(nseq * n / dt, 2), "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} x {nseq} sequences of configs[2] (KV 8192, 26 kept blocks per kv-head); "
+                      f"oracle/tasft_oracle.py:bsa_decode, {dt:.1f} s"}
+
+
+def cpu_gate_sample(budget_s: float = 3.0):
+    """Oracle AttnGate.forward (fp32, attn_gate.py:377-485) on one (sequence, kv-group)
+    chunk of the configs[1] workload; rate in algorithmic bytes (bf16 |Q| + |K|) per s."""
+    import oracle as O  # noqa: PLC0415  (CPU baseline leg)
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = CFG
+    grp = c["Hq"] // c["Hk"]
+    g = torch.Generator().manual_seed(78)
+    q = torch.randn(1, grp, c["S"], c["D"], generator=g)
+    k = torch.randn(1, 1, c["S"], c["D"], generator=g)
+    hid = max(32, c["D"] // 4)
+    w_in = torch.randn(hid, 2 * c["D"], generator=g) * 0.05
+    b_in = torch.zeros(hid)
+    w_out = torch.randn(1, hid, generator=g) * 0.01
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        O.gate_forward_gqa(q, k, w_in, b_in, w_out, c["block"], 0.5)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    nbytes = (q.numel() + k.numel()) * 2
+    return {"value": round(nbytes * n / dt / 1e9, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} x one (sequence, kv-head group) chunk: 4 q-heads + 1 kv-head, S=4096, D=128, fp32; "
+                      f"oracle/tasft_oracle.py:gate_forward_gqa, {dt:.1f} s"}
+
+
+def cpu_target_sample(budget_s: float = 3.0):
+    """Oracle gate target (bf16 training scores, max-pool, softmax; tasft_attention.py:427-443 +
+    objectives.py:128-185) for single heads of the configs[4] workload."""
+    import oracle as O  # noqa: PLC0415  (CPU baseline leg)
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = CFG
+    g = torch.Generator().manual_seed(79)
+    q = torch.randn(1, 1, c["S"], c["D"], generator=g).bfloat16()
+    k = torch.randn(1, 1, c["S"], c["D"], generator=g).bfloat16()
+    nb = c["S"] // c["block"]
+    flop = nb * (nb + 1) // 2 * 2 * c["block"] * c["block"] * c["D"]
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        O.gate_target_from_qk(q, k, c["block"])
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(flop * n / dt / 1e12, 6), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} x one head (S=4096, D=128, bf16 scores); oracle/tasft_oracle.py:gate_target_from_qk, "
+                      f"{dt:.1f} s"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -378,6 +638,11 @@ def run_ours(args):
                                 "traffic": traffic.get("target"), "peak_src": f"bf16 burst, {peaks['src']}",
                                 "algorithmic": f"{tflop / 1e9:.1f} GFLOP per step (causal 64x64 tiles x 2*64*64*128 "
                                                "x B x Hq)"}}
+
+    # ---------------- drop-in form, reference Triton kernel, gate training step, strong C2 ----------------
+    dropin = bench_dropin(q, k, v, _gate, kern, flush, ws, args, peaks)
+    gate_train = bench_gate_train(q, k, flush, ws, args)
+    strong_c2 = bench_strong_c2(q, k, v, mask, rank, ws, flush, args, peaks) if ws > 1 else None
 
     # ---------------- e2e through the public API with host buffers ----------------
     qh = q.cpu().pin_memory()
@@ -513,9 +778,14 @@ def run_ours(args):
                    "tok_s": round(lc["B"] / (ms_l * 1e-3), 1)}
     del kl_loc, vl_loc
 
+    qwen_prefill = bench_qwen_prefill(rank, ws, dev, flush, args, peaks)
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         cpu = cpu_prefill_sample(budget_s=args.cpu_budget)
+        decode["cpu_baseline"] = cpu_decode_sample()
+        gate_info["cpu_baseline"] = cpu_gate_sample()
+        target_info["cpu_baseline"] = cpu_target_sample()
 
     if rank == 0:
         line = {
@@ -539,11 +809,16 @@ def run_ours(args):
             "gate": gate_info,
             "gate_target": target_info,
             "long_decode": long_decode,
+            "prefill_dropin": dropin,
+            "qwen_prefill": qwen_prefill,
+            "gate_train": gate_train,
             "gpu_launches": launches * args.steps,
             "gpu_launches_per_step": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
+        if strong_c2 is not None:
+            line["strong_c2"] = strong_c2
         print(json.dumps(line))
     if ws > 1:
         import torch.distributed as dist  # noqa: PLC0415
@@ -599,6 +874,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-triton", action="store_true", help="skip timing the reference Triton kernel")
     ap.add_argument("--only", choices=["prefill", "decode", "paged", "gate", "target"],
                     help="profiling driver: run `--steps` launches of one kernel family, print nothing else")
     args = ap.parse_args()

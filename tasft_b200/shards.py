@@ -48,6 +48,22 @@ def unit_weights(kept: KeptBlocks, hk: int) -> torch.Tensor:
     return cnt.reshape(B, hk, hm // hk, -1).sum(dim=(2, 3)).reshape(-1)
 
 
+def unit_slices(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kept: KeptBlocks, units):
+    """The Q/K/V slices and kept lists of the (sequence, kv-head) units ``units`` (ids
+    ``b * Hk + hk``) as one batch: ``q [U, grp, S, D]``, ``k, v [U, 1, S, D]`` and lists
+    ``[U, mg, NB, NB]`` (mg = 1 for kv-head lists, grp for per-q-head lists)."""
+    Hk = k.shape[1]
+    grp = q.shape[1] // Hk
+    hm = kept.idx.shape[1]
+    mg = hm // Hk
+    ids = torch.as_tensor(list(units), dtype=torch.long, device=q.device)
+    b, h = ids // Hk, ids % Hk
+    hq = (h[:, None] * grp + torch.arange(grp, device=q.device)[None, :])
+    hl = (h[:, None] * mg + torch.arange(mg, device=q.device)[None, :])
+    return (q[b[:, None], hq], k[b, h].unsqueeze(1), v[b, h].unsqueeze(1),
+            KeptBlocks(kept.idx[b[:, None], hl].contiguous(), kept.cnt[b[:, None], hl].contiguous()))
+
+
 def prefill_units(kern, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kept: KeptBlocks, units,
                   causal: bool = True) -> torch.Tensor:
     """Prefill of the (sequence, kv-head) units ``units`` only (ids ``b * Hk + hk``), as
@@ -55,18 +71,7 @@ def prefill_units(kern, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kept:
     each unit's group. A rank of a sharded prefill passes the units ``assign_units`` gave
     it; the tensors may be the full batch or just those units' slices gathered by the
     caller (then ``units`` are indices into that smaller batch)."""
-    Hk = k.shape[1]
-    grp = q.shape[1] // Hk
-    hm = kept.idx.shape[1]
-    mg = hm // Hk  # list heads per kv-head (1: kv-head lists, grp: per-q-head lists)
-    ids = torch.as_tensor(list(units), dtype=torch.long, device=q.device)
-    b, h = ids // Hk, ids % Hk
-    hq = (h[:, None] * grp + torch.arange(grp, device=q.device)[None, :])  # [U, grp]
-    hl = (h[:, None] * mg + torch.arange(mg, device=q.device)[None, :])    # [U, mg]
-    qu = q[b[:, None], hq]              # [U, grp, S, D]
-    ku = k[b, h].unsqueeze(1)           # [U, 1, S, D]
-    vu = v[b, h].unsqueeze(1)
-    ku_kept = KeptBlocks(kept.idx[b[:, None], hl].contiguous(), kept.cnt[b[:, None], hl].contiguous())
+    qu, ku, vu, ku_kept = unit_slices(q, k, v, kept, units)
     return kern.forward(qu, ku, vu, ku_kept, causal=causal)
 
 
@@ -222,5 +227,5 @@ class SplitKVDecoder:
 
 
 __all__ = ["assign_units", "block_range", "gather_partials", "local_kept", "local_kv_len", "long_context_decode",
-           "prefill_units", "qblock_ranges", "restrict_qblocks", "scatter_units", "unit_weights",
+           "prefill_units", "qblock_ranges", "restrict_qblocks", "scatter_units", "unit_slices", "unit_weights",
            "SplitKVDecoder"]
