@@ -227,7 +227,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     int gk = 0;  // global block counter (ring position)
     bool ok = true;
     for (int u = 0; ok; ++u) {
-      const int tile = blockIdx.x + u * gridDim.x;
+      // tiles run heaviest first; the CTA order snakes (0..G-1, then G-1..0, ...) so every
+      // CTA's sum of tile sizes comes out about equal
+      const int tile = u * gridDim.x + ((u & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
       const int lb = u & 1;
       if (u >= 2 && !warp_wait(&list_empty[lb], ((u >> 1) - 1) & 1)) {
         set_err(a.err, TASFT_DEVERR_TIMEOUT | (1 << (8 + 1)));

@@ -336,29 +336,65 @@ __global__ void bwd_cols_kernel(tasft_gate_bwd_args a, const float* A, const flo
   }
 }
 
-// weight grads: CTA per (h, half); threads over d. half 0: rows/pq, half 1: cols/pk
-__global__ void bwd_weights_kernel(tasft_gate_bwd_args a, const float* dA, const float* dwo, const float* dC) {
-  const int h = blockIdx.x, half = blockIdx.y;
-  const int64_t n = half == 0 ? (int64_t)a.B * a.Hq * a.NBq : (int64_t)a.B * a.Hk * a.NBk;
-  const float* g = half == 0 ? dA : dC;
-  const float* x = half == 0 ? a.pooled_q : a.pooled_k;
-  for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+// Weight gradients dW_q = dA^T pq, dW_k = dC^T pk, db = sum dA, dw_out = sum dwo, as two
+// deterministic stages: each CTA reduces one chunk of kWChunk rows into partials (the
+// rows staged in shared memory), then one thread per output sums the chunks in order.
+constexpr int kWChunk = 64;
+
+__global__ void bwd_wpart_kernel(tasft_gate_bwd_args a, const float* dA, const float* dwo, const float* dC,
+                                 int chunks_q, float* part, float* part_b) {
+  extern __shared__ float sh[];
+  const int hid = a.hidden, D = a.D;
+  const bool isq = (int)blockIdx.x < chunks_q;
+  const int chunk = isq ? blockIdx.x : blockIdx.x - chunks_q;
+  const int64_t n = isq ? (int64_t)a.B * a.Hq * a.NBq : (int64_t)a.B * a.Hk * a.NBk;
+  const int64_t r0 = (int64_t)chunk * kWChunk;
+  const int rows = (int)(n - r0 < kWChunk ? n - r0 : kWChunk);
+  const float* g = (isq ? dA : dC) + r0 * hid;
+  const float* x = (isq ? a.pooled_q : a.pooled_k) + r0 * D;
+  float* sg = sh;                  // [kWChunk][hid]
+  float* sx = sh + kWChunk * hid;  // [kWChunk][D]
+  for (int i = threadIdx.x; i < rows * hid; i += blockDim.x) sg[i] = g[i];
+  for (int i = threadIdx.x; i < rows * D; i += blockDim.x) sx[i] = x[i];
+  __syncthreads();
+  float* out = part + (int64_t)blockIdx.x * hid * D;
+  for (int o = threadIdx.x; o < hid * D; o += blockDim.x) {
+    const int h = o / D, d = o % D;
     float s = 0.f;
-    for (int64_t r = 0; r < n; ++r) s = fmaf(g[r * a.hidden + h], x[r * a.D + d], s);
-    a.d_w_in[(int64_t)h * 2 * a.D + half * a.D + d] = s;
+    for (int r = 0; r < rows; ++r) s = fmaf(sg[r * hid + h], sx[r * D + d], s);
+    out[o] = s;
   }
-  if (half == 0 && threadIdx.x < 32) {
-    float sb = 0.f, sw = 0.f;
-    for (int64_t r = threadIdx.x; r < n; r += 32) {
-      sb += dA[r * a.hidden + h];
-      sw += dwo[r * a.hidden + h];
+  if (isq) {
+    for (int h = threadIdx.x; h < hid; h += blockDim.x) {
+      float sb = 0.f, sw = 0.f;
+      for (int r = 0; r < rows; ++r) {
+        sb += sg[r * hid + h];
+        sw += dwo[(r0 + r) * hid + h];
+      }
+      part_b[((int64_t)chunk * hid + h) * 2] = sb;
+      part_b[((int64_t)chunk * hid + h) * 2 + 1] = sw;
     }
-    sb = warp_sum(sb);
-    sw = warp_sum(sw);
-    if (threadIdx.x == 0) {
-      a.d_b_in[h] = sb;
-      a.d_w_out[h] = sw;
-    }
+  }
+}
+
+__global__ void bwd_wsum_kernel(tasft_gate_bwd_args a, int chunks_q, int chunks_k, const float* part,
+                                const float* part_b) {
+  const int hid = a.hidden, D = a.D;
+  const int64_t nw = (int64_t)hid * 2 * D;
+  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o < nw) {
+    const int h = (int)(o / (2 * D)), c = (int)(o % (2 * D));
+    const bool isq = c < D;
+    const int d = isq ? c : c - D;
+    const int c0 = isq ? 0 : chunks_q, nc = isq ? chunks_q : chunks_k;
+    float s = 0.f;
+    for (int k = 0; k < nc; ++k) s += part[((int64_t)(c0 + k) * hid + h) * D + d];
+    a.d_w_in[o] = s;
+  } else if (o < nw + 2 * hid) {
+    const int t = (int)(o - nw), h = t >> 1, which = t & 1;
+    float s = 0.f;
+    for (int k = 0; k < chunks_q; ++k) s += part_b[((int64_t)k * hid + h) * 2 + which];
+    (which ? a.d_w_out : a.d_b_in)[h] = s;
   }
 }
 
@@ -532,7 +568,11 @@ extern "C" int64_t tasft_gate_bwd_workspace_size(int32_t B, int32_t Hq, int32_t 
   if (B <= 0 || Hq <= 0 || Hk <= 0 || NBq <= 0 || NBk <= 0 || hidden <= 0) return -1;
   const int64_t rq = (int64_t)B * Hq * NBq, rk = (int64_t)B * Hk * NBk;
   const int64_t floats = rq * hidden * 3 + rk * hidden * 2;  // A, dA, dwo, Ct, dC
-  return (floats * 4 + 1023) / 256 * 256;
+  // weight-gradient partials: one [hidden, D] slab per row chunk + (db, dw_out) per q chunk
+  // (D is not an argument here; the partials are sized for the largest supported D, 256)
+  const int64_t cq = (rq + 63) / 64, ck = (rk + 63) / 64;
+  const int64_t part = (cq + ck) * hidden * 256 + cq * hidden * 2;
+  return ((floats + part) * 4 + 1023) / 256 * 256;
 }
 
 extern "C" int tasft_gate_bwd(const tasft_gate_bwd_args* ap, tasft_stream_t stream) {
@@ -543,6 +583,7 @@ extern "C" int tasft_gate_bwd(const tasft_gate_bwd_args* ap, tasft_stream_t stre
     return TASFT_ERR_INVALID_ARG;
   if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.NBq <= 0 || a.NBk <= 0 || a.D <= 0 || a.hidden <= 0 || a.Hq % a.Hk)
     return TASFT_ERR_INVALID_ARG;
+  if (a.D > 256 || a.hidden > 256) return TASFT_ERR_UNSUPPORTED;
   const int64_t need = tasft_gate_bwd_workspace_size(a.B, a.Hq, a.Hk, a.NBq, a.NBk, a.hidden);
   if (!a.workspace || a.workspace_bytes < need) return TASFT_ERR_WORKSPACE;
   const int64_t rq = (int64_t)a.B * a.Hq * a.NBq, rk = (int64_t)a.B * a.Hk * a.NBk;
@@ -555,8 +596,17 @@ extern "C" int tasft_gate_bwd(const tasft_gate_bwd_args* ap, tasft_stream_t stre
   bwd_project_kernel<<<(unsigned)(rq + rk), 64, 0, st>>>(a, A, Ct);
   bwd_rows_kernel<<<ceil_div(rq, 8), 256, 0, st>>>(a, A, Ct, dA, dwo);
   bwd_cols_kernel<<<ceil_div(rk, 8), 256, 0, st>>>(a, A, Ct, dC);
-  bwd_weights_kernel<<<dim3(a.hidden, 2), 128, 0, st>>>(a, dA, dwo, dC);
+  const int cq = (int)ceil_div(rq, kWChunk), ck = (int)ceil_div(rk, kWChunk);
+  float* part = dC + rk * a.hidden;
+  float* part_b = part + (int64_t)(cq + ck) * a.hidden * a.D;
+  const size_t wsm = (size_t)kWChunk * (a.hidden + a.D) * sizeof(float);
+  if (wsm > 48 * 1024 && cudaFuncSetAttribute(bwd_wpart_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)wsm) != cudaSuccess)
+    return TASFT_ERR_CUDA;
+  bwd_wpart_kernel<<<cq + ck, 256, wsm, st>>>(a, dA, dwo, dC, cq, part, part_b);
+  const int64_t nout = (int64_t)a.hidden * 2 * a.D + 2 * a.hidden;
+  bwd_wsum_kernel<<<(unsigned)ceil_div(nout, 256), 256, 0, st>>>(a, cq, ck, part, part_b);
   bwd_inputs_kernel<<<(unsigned)(rq + rk), 128, 0, st>>>(a, dA, dC);
-  count_launch(5);
+  count_launch(6);
   return launch_status();
 }
