@@ -152,9 +152,7 @@ typedef struct {
   const int32_t* kept_cnt;/* [B, Hm, NB] */
   int32_t Hm;             /* heads of the lists: Hq (per q-head) or Hk (per kv-head) */
   int32_t* err;           /* optional device error word */
-  int32_t force_simt;     /* kernel choice for testing: 0 = fastest that applies; 1 = the CUDA-core
-                             kernel; 2 = the two-slot tcgen05 kernel even where the quad kernel
-                             (per-kv-head lists, GQA group >= 3) applies */
+  int32_t force_simt;     /* 1 = use the CUDA-core kernel even where tcgen05 applies (testing) */
 } tasft_prefill_args;
 TASFT_API int tasft_bsa_prefill_fwd(const tasft_prefill_args* args, tasft_stream_t stream);
 

@@ -25,8 +25,6 @@ int prefill_simt(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu
 // Returns TASFT_ERR_UNSUPPORTED when the tcgen05 kernel does not cover the shape.
 // `cu` (cu_seqlens, B + 1 entries) and `total` describe packed sequences; nullptr / 0 otherwise.
 int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu = nullptr, int total = 0);
-// Quad-tile tcgen05 kernel for per-kv-head lists with GQA groups >= 3 (padded layout only).
-int prefill_quad(const tasft_prefill_args& a, cudaStream_t st);
 }  // namespace tasft
 
 using namespace tasft;
@@ -41,11 +39,7 @@ extern "C" int tasft_bsa_prefill_fwd(const tasft_prefill_args* ap, tasft_stream_
     return TASFT_ERR_INVALID_ARG;
   if (a.block != 32 && a.block != 64 && a.block != 128) return TASFT_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (a.force_simt == 0) {
-    const int rc = prefill_quad(a, st);
-    if (rc != TASFT_ERR_UNSUPPORTED) return rc;
-  }
-  if (a.force_simt != 1) {
+  if (!a.force_simt) {
     const int rc = prefill_tc(a, st);
     if (rc != TASFT_ERR_UNSUPPORTED) return rc;
   }
@@ -63,7 +57,7 @@ extern "C" int tasft_bsa_prefill_varlen_fwd(const tasft_prefill_varlen_args* vp,
     return TASFT_ERR_INVALID_ARG;
   if (a.block != 32 && a.block != 64 && a.block != 128) return TASFT_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (a.force_simt != 1) {
+  if (!a.force_simt) {
     const int rc = prefill_tc(a, st, vp->cu_seqlens, vp->total);
     if (rc != TASFT_ERR_UNSUPPORTED) return rc;
   }
