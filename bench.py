@@ -615,7 +615,7 @@ def run_ours(args):
     ms_g = statistics.mean(t_gate)
     gbytes = (q.numel() + k.numel()) * 2
     gate_info = {"ms_per_step": round(ms_g, 4), "timing": "CUDA graph replay of AttnGate.forward",
-                 "kernels": "gate_pool_kernel + gate_project_kernel + gate_pair_slab_kernel",
+                 "kernels": "gate_pool_project_fused_kernel + gate_pair_slab_kernel",
                  "roofline": {"bound": "hbm", "achieved": round(gbytes / (ms_g * 1e-3) / 1e9, 1),
                               "peak": peaks["hbm_gbs"], "unit": "GB/s",
                               "frac": round(gbytes / (ms_g * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),

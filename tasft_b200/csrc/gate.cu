@@ -9,6 +9,10 @@
 // small kernel projects the means), and the pair kernel only evaluates
 // w_out . relu(a_i + c_j). Same maths; the fp32 summation order differs from the
 // reference's single 2D-long dot product.
+#include <algorithm>
+#include <cstdlib>
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace tasft {
@@ -109,6 +113,10 @@ __global__ void __launch_bounds__(kPoolThreads) gate_pool_project_kernel(tasft_g
   }
 }
 
+// Programmatic dependent launch: a CTA whose streaming is done lets the next kernel on the
+// stream (the pair kernel, which waits with griddepcontrol.wait) start launching.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // Kernel 1 fast path, two passes.
 // 1a: one thread per (tensor, b, head, block, 16-byte column vector) sums that column over
@@ -179,6 +187,107 @@ __global__ void __launch_bounds__(kPoolThreads, 6) gate_pool_kernel(tasft_gate_a
     *reinterpret_cast<float4*>(out + e) = make_float4(f[e] * inv, f[e + 1] * inv, f[e + 2] * inv, f[e + 3] * inv);
 }
 
+
+// Pool and project in one pass. Same pooling as gate_pool_kernel (one thread per 16-byte
+// column of a block, CV = D / EPV lanes per block, contiguous in the warp); then each lane
+// forms the partial products of its EPV means with all HID rows of its W_in half (read
+// through L1: the CV lanes of a block read one contiguous row of W per unit), and a
+// butterfly reduce-scatter over the block's CV lanes sums them: lane c ends with the
+// HID / CV units [c * HID / CV, (c + 1) * HID / CV). Saves the means' round trip through
+// HBM and a kernel boundary.
+template <typename T, int EPV, int CV, int HID>
+__global__ void __launch_bounds__(kPoolThreads, 3) gate_pool_project_fused_kernel(tasft_gate_args a, float* A,
+                                                                                  float* Ct, int NBq, int NBk) {
+  constexpr int D = EPV * CV;
+  constexpr int NOUT = HID / CV;  // units per lane after the reduction
+  static_assert(HID % CV == 0 && (CV & (CV - 1)) == 0 && CV <= 32, "shape");
+  int t = blockIdx.x * kPoolThreads + threadIdx.x;
+  const int nq = a.B * a.Hq * NBq * CV;
+  const int nk = a.B * a.Hk * NBk * CV;
+  const bool live = t < nq + nk;
+  if (!live) t = nq + nk - 1;  // idle lanes shadow the last block so the shuffles stay full-warp
+  const bool isq = t < nq;
+  if (!isq) t -= nq;
+  const int c = t & (CV - 1);
+  const int row = t / CV;  // (b * H + h) * NB + blk
+  const int H = isq ? a.Hq : a.Hk, NB = isq ? NBq : NBk, S = isq ? a.Sq : a.Sk;
+  const int blk = row % NB, bh = row / NB;
+  const int h = bh % H, b = bh / H;
+  const int64_t* st = isq ? a.q_stride : a.k_stride;
+  const T* p = reinterpret_cast<const T*>(isq ? a.q : a.k) + b * st[0] + h * st[1] +
+               (int64_t)blk * a.block * st[2] + c * EPV;
+  const int rows = min(a.block, S - blk * a.block);  // padding rows count as zeros
+  const int64_t rs = st[2];
+  float f[EPV];
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) add_bf16x8(__ldg(reinterpret_cast<const uint4*>(p + r * rs)), acc);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float((uint32_t)acc[i]);
+      f[2 * i + 1] = __uint_as_float((uint32_t)(acc[i] >> 32));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) f[e] = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) {
+      float g[EPV];
+      Vec16<T>::unpack(__ldg(reinterpret_cast<const uint4*>(p + r * rs)), g);
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) f[e] += g[e];
+    }
+  }
+  // this CTA's streaming is done: the pair kernel may launch (it waits for this grid)
+  pdl_trigger();
+  const float inv = 1.0f / (float)a.block;
+#pragma unroll
+  for (int e = 0; e < EPV; ++e) f[e] *= inv;
+  float* pooled = isq ? a.pooled_q : a.pooled_k;
+  if (pooled && live) {
+    float* out = pooled + (int64_t)row * D + c * EPV;
+#pragma unroll
+    for (int e = 0; e < EPV; e += 4) *reinterpret_cast<float4*>(out + e) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
+  }
+  // partial products of this lane's EPV means with every unit
+  float v[HID];
+  const float* w = a.w_in + (isq ? 0 : D) + c * EPV;
+#pragma unroll
+  for (int j = 0; j < HID; ++j) {
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPV; e += 4) {
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (int64_t)j * 2 * D + e));
+      s = fmaf(wv.x, f[e], fmaf(wv.y, f[e + 1], fmaf(wv.z, f[e + 2], fmaf(wv.w, f[e + 3], s))));
+    }
+    v[j] = s;
+  }
+  // butterfly reduce-scatter over the CV lanes of this block
+  int n = HID;
+#pragma unroll
+  for (int d = CV / 2; d >= 1; d >>= 1) {
+    const bool upper = (c & d) != 0;
+    n >>= 1;
+#pragma unroll
+    for (int i = 0; i < HID / 2; ++i) {
+      if (i < n) {
+        const float send = upper ? v[i] : v[i + n];
+        const float keep = upper ? v[i + n] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+      }
+    }
+  }
+  if (!live) return;
+  const int j0 = c * NOUT;  // lane c holds units [j0, j0 + NOUT)
+  if (isq) {
+#pragma unroll
+    for (int i = 0; i < NOUT; ++i) A[(int64_t)row * HID + j0 + i] = v[i] + a.b_in[j0 + i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < NOUT; ++i) Ct[((int64_t)bh * HID + j0 + i) * NB + blk] = v[i];
+  }
+}
 
 template <int HID>
 __global__ void __launch_bounds__(kPoolThreads) gate_project_kernel(tasft_gate_args a, const float* mq,
@@ -326,10 +435,11 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_kernel(tasft_gate_
 // The same row computation with the kv-head's projected K rows (Ct slab, hid x NBk)
 // staged in shared memory once per CTA: a CTA takes 8 q-rows of one (b, kv-head) (the
 // group's q-heads read the same slab), one warp per row, lanes over k-blocks.
-constexpr int kSlabRows = 8;  // one row per warp: many CTAs for latency hiding
+constexpr int kSlabRowsDefault = 16;  // q-rows per CTA (4 per warp): the Ct slab staging is amortised
 
 __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_slab_kernel(tasft_gate_args a, const float* A,
-                                                                          const float* Ct, int NBq, int NBk) {
+                                                                          const float* Ct, int NBq, int NBk,
+                                                                          int kSlabRows) {
   extern __shared__ float sm[];  // ct [hid][NBk], arows [kSlabRows][hid], wout [hid]
   const int hid = a.hidden;
   const int grp = a.Hq / a.Hk;
@@ -343,6 +453,9 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_slab_kernel(tasft_
   float* arows = sm + hid * NBk;
   float* wout = arows + kSlabRows * hid;
   const float* src = Ct + (int64_t)bk * hid * NBk;
+  // launched early (programmatic dependent launch) behind the pooling kernel: wait for its
+  // results; a no-op when launched normally
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll 8
   for (int x = threadIdx.x; x < hid * NBk; x += blockDim.x) ct[x] = __ldg(src + x);
   for (int x = threadIdx.x; x < nrows * hid; x += blockDim.x) {
@@ -470,7 +583,20 @@ static int launch_pool(const tasft_gate_args& a, float* A, float* Ct, float* mq,
   // projection's shared memory (D * (hidden + 256 / hidden) floats) stays under 48 KB
   const int CV = a.D / EPV;
   const int64_t nthreads = ((int64_t)a.B * a.Hq * NBq + (int64_t)a.B * a.Hk * NBk) * CV;
-  if (vec_ok && (CV & (CV - 1)) == 0 && a.D % 4 == 0 && a.D <= 128 && (a.hidden == 32 || a.hidden == 64) &&
+  const bool pooled_ok = (!a.pooled_q || aligned16(a.pooled_q)) && (!a.pooled_k || aligned16(a.pooled_k)) &&
+                         aligned16(a.w_in);
+  if (vec_ok && EPV == 8 && (a.D == 64 || a.D == 128) && (a.hidden == 32 || a.hidden == 64) && pooled_ok &&
+      nthreads < (1LL << 31) - kPoolThreads && !std::getenv("TASFT_GATE_UNFUSED")) {
+    const unsigned blocks = (unsigned)ceil_div(nthreads, kPoolThreads);
+    auto go = [&](auto kern) { kern<<<blocks, kPoolThreads, 0, st>>>(a, A, Ct, NBq, NBk); };
+    if (a.D == 128) {
+      if (a.hidden == 32) go(gate_pool_project_fused_kernel<T, 8, 16, 32>);
+      else go(gate_pool_project_fused_kernel<T, 8, 16, 64>);
+    } else {
+      if (a.hidden == 32) go(gate_pool_project_fused_kernel<T, 8, 8, 32>);
+      else go(gate_pool_project_fused_kernel<T, 8, 8, 64>);
+    }
+  } else if (vec_ok && (CV & (CV - 1)) == 0 && a.D % 4 == 0 && a.D <= 128 && (a.hidden == 32 || a.hidden == 64) &&
       nthreads < (1LL << 31) - kPoolThreads && aligned16(mq) && aligned16(mk)) {
     int lcv = 0;
     while ((1 << lcv) < CV) ++lcv;
@@ -521,6 +647,8 @@ extern "C" int tasft_gate_mask_build(const tasft_gate_args* ap, tasft_stream_t s
     default: return TASFT_ERR_UNSUPPORTED;
   }
   if (rc != TASFT_OK) return rc;
+  int kSlabRows = kSlabRowsDefault;
+  if (const char* e = std::getenv("TASFT_GATE_SLAB_ROWS")) kSlabRows = std::max(1, std::atoi(e));  // tuning aid
   const size_t slab = (size_t)(a.hidden * NBk + kSlabRows * a.hidden + a.hidden) * sizeof(float);
   if (slab <= 96 * 1024) {
     auto kern = gate_pair_slab_kernel;
@@ -528,7 +656,19 @@ extern "C" int tasft_gate_mask_build(const tasft_gate_args* ap, tasft_stream_t s
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slab) != cudaSuccess)
       return TASFT_ERR_CUDA;
     const int64_t grid = (int64_t)a.B * a.Hk * ceil_div((int64_t)(a.Hq / a.Hk) * NBq, kSlabRows);
-    kern<<<(unsigned)grid, kRowsPerCta * 32, slab, st>>>(a, A, Ct, NBq, NBk);
+    // programmatic dependent launch: the pair kernel's launch overlaps the pooling tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kRowsPerCta * 32);
+    cfg.dynamicSmemBytes = slab;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = std::getenv("TASFT_GATE_NO_PDL") ? 0 : 1;  // comparison aid
+    if (cudaLaunchKernelEx(&cfg, kern, a, (const float*)A, (const float*)Ct, NBq, NBk, kSlabRows) != cudaSuccess)
+      return launch_status();
   } else {
     const int64_t rows = (int64_t)a.B * a.Hq * NBq;
     const size_t smem = (size_t)(kRowsPerCta + 1) * a.hidden * sizeof(float);
