@@ -748,35 +748,51 @@ def run_ours(args):
     ql = torch.randn(lc["B"], lc["Hq"], lc["D"], device=dev, dtype=torch.bfloat16, generator=g)
     nbl = lc["L"] // lc["block"]
     lo, hi = SH.block_range(nbl, rank, ws)
-    kl_loc = torch.randn(lc["B"], lc["Hk"], (hi - lo) * lc["block"], lc["D"], device=dev, dtype=torch.bfloat16,
-                         generator=g)
-    vl_loc = torch.randn_like(kl_loc)
+    kl_full = torch.randn(lc["B"], lc["Hk"], lc["L"], lc["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    vl_full = torch.randn_like(kl_full)
+    kl_loc = kl_full[:, :, lo * lc["block"]: hi * lc["block"]].contiguous()
+    vl_loc = vl_full[:, :, lo * lc["block"]: hi * lc["block"]].contiguous()
     kvl = torch.full((lc["B"],), lc["L"], dtype=torch.int32, device=dev)
     lmask = M.decode_mask(torch.rand(lc["B"], lc["Hk"], nbl, device=dev, generator=g), (kvl + 63) // 64,
                           lc["density"], nbl)
     lkept = T.KeptBlocks(*M.lists_from_mask(lmask))
-    ltiming = "CUDA graph replay"
+    long_extra = {}
     if ws > 1:
-        # eager (capturing the NCCL all-gather in a CUDA graph stalled the ranks here), with
-        # the decoder's buffers and this rank's rebased kept lists kept across steps
-        dec = SH.SplitKVDecoder(lc["B"], lc["Hq"], lc["Hk"], lc["D"], dev)
+        # the step (local decode over this rank's KV range + merge of all ranks' partials over
+        # peer memory) replayed from a CUDA graph: no NCCL call and no host work per token
+        dec = SH.SplitKVDecoder(lc["B"], lc["Hq"], lc["Hk"], lc["D"], dev, exchange="peer")
         lloc = dec.local(lkept, lo, hi - lo)
-        lstep = lambda: dec(ql, kl_loc, vl_loc, kvl, lkept, lo, local=lloc)  # noqa: E731
-        ltiming = "eager calls incl. the NCCL all-gather"
+        lstep = graphed(lambda: dec(ql, kl_loc, vl_loc, kvl, lkept, lo, local=lloc))
+        ltiming = "CUDA graph replay (local split decode + peer-memory merge kernel)"
+        # the NCCL all-gather + combine path, eager, for comparison
+        dec_n = SH.SplitKVDecoder(lc["B"], lc["Hq"], lc["Hk"], lc["D"], dev, exchange="nccl")
+        t_n = time_steps(lambda: dec_n(ql, kl_loc, vl_loc, kvl, lkept, lo, local=lloc), args.steps, args.warmup,
+                         flush, ws)
+        long_extra["ms_per_token_nccl_eager"] = round(max_over_ranks(statistics.mean(t_n), ws), 4)
     else:
         # one GPU: the step replayed from a CUDA graph, as a serving loop would run it (its
         # Python launch path takes longer than the ~20 us of kernels)
         lstep = graphed(lambda: T.bsa_decode(ql, kl_loc, vl_loc, kvl, lkept, lc["block"]))
+        ltiming = "CUDA graph replay"
     t_long = time_steps(lstep, args.steps, args.warmup, flush, ws)
     ms_l = max_over_ranks(statistics.mean(t_long), ws)
+    if ws > 1:
+        # parity: the merged token against a one-rank decode of the whole cache, on every rank
+        lstep()
+        ref = T.bsa_decode(ql, kl_full, vl_full, kvl, lkept, lc["block"])
+        err = (dec.out.float() - ref.float()).abs().max().item()
+        long_extra["max_abs_err_vs_one_rank"] = round(max_over_ranks(err, ws), 6)
+        long_extra["device_err_word"] = int(max_over_ranks(float(dec.peer.err.item()), ws))
+        barrier(ws)
+        dec.peer.close()
     long_decode = {"config": "BASELINE configs[3] decode: B=1, Hq=28, Hk=4, KV=32768, D=128, 90% block sparsity "
                              f"({int(lkept.cnt.float().mean().item())} of {nbl} blocks kept per kv-head)",
-                   "split": f"KV positions over {ws} rank(s); partials all-gathered + log-sum-exp combine"
+                   "split": f"KV positions over {ws} rank(s); partials merged over peer memory (CUDA IPC)"
                             if ws > 1 else "one GPU",
                    "scaling": "strong", "ms_per_token": round(ms_l, 4),
                    "timing": ltiming,
-                   "tok_s": round(lc["B"] / (ms_l * 1e-3), 1)}
-    del kl_loc, vl_loc
+                   "tok_s": round(lc["B"] / (ms_l * 1e-3), 1), **long_extra}
+    del kl_loc, vl_loc, kl_full, vl_full
 
     qwen_prefill = bench_qwen_prefill(rank, ws, dev, flush, args, peaks)
 

@@ -28,6 +28,8 @@
  *   tasft_gate_target_fwd      TASFTAttention scores + compute_gate_target
  *                              tasft/modules/tasft_attention.py:427-458,
  *                              tasft/training/objectives.py:128-185
+ *   tasft_attention_train_fwd  TASFTAttention._training_forward scores + softmax + P V and
+ *                              compute_gate_target, fused (tasft_attention.py:427-466)
  *   tasft_gate_target_from_scores  compute_gate_target on a score tensor
  *                              tasft/training/objectives.py:128-185
  *   tasft_gate_loss_fwd_bwd    compute_gate_loss + compute_sparsity_loss (+ grad)
@@ -246,6 +248,38 @@ typedef struct {
 } tasft_combine_args;
 TASFT_API int tasft_bsa_decode_combine(const tasft_combine_args* args, tasft_stream_t stream);
 
+/* Cross-GPU merge of split-KV decode partials over peer memory, in place of an NCCL
+ * all-gather + tasft_bsa_decode_combine. No counterpart in the reference (it has no
+ * sparse decode). Each rank owns a mailbox (tasft_peer_alloc of
+ * tasft_peer_mailbox_bytes(world, rows, D) bytes, zeroed) and maps every other rank's
+ * mailbox with tasft_ipc_handle / tasft_ipc_open (CUDA IPC; one process per GPU). A call
+ * pushes this rank's partial into every mailbox with plain stores, raises its flag in each,
+ * waits for all ranks' flags in its own mailbox (bounded by timeout_ns; on expiry
+ * TASFT_DEVERR_TIMEOUT is OR-ed into *err and the exchange must be rebuilt) and writes
+ * the merged output. Every rank must make the same sequence of calls; the per-rank epoch
+ * counter lives on the device, so a step that contains the call can be replayed from a
+ * CUDA graph. */
+typedef struct {
+  const float* part_o;    /* [rows, D] this rank's normalised partial output */
+  const float* part_ml;   /* [rows, 2] its (m, l), base e */
+  int64_t rows;           /* B * Hq */
+  int32_t D;
+  int32_t world, rank;
+  void* const* mailboxes; /* device array [world] of device pointers: rank r's mailbox (own or IPC-mapped) */
+  uint32_t* epoch;        /* device scalar of this rank, zero before the first call */
+  void* out;              /* [rows, D] dtype */
+  int32_t dtype;
+  uint64_t timeout_ns;    /* bound of the wait for the other ranks */
+  int32_t* err;           /* optional device error word */
+} tasft_peer_combine_args;
+TASFT_API int64_t tasft_peer_mailbox_bytes(int32_t world, int64_t rows, int32_t D);
+TASFT_API int tasft_peer_alloc(int64_t bytes, void** ptr);
+TASFT_API int tasft_peer_free(void* ptr);
+TASFT_API int tasft_ipc_handle(void* ptr, uint8_t* handle64);
+TASFT_API int tasft_ipc_open(const uint8_t* handle64, void** ptr);
+TASFT_API int tasft_ipc_close(void* ptr);
+TASFT_API int tasft_peer_combine(const tasft_peer_combine_args* args, tasft_stream_t stream);
+
 /* ------------------------------------------------------------------------- */
 /* Training-time gate target, losses and gate backward                       */
 /* ------------------------------------------------------------------------- */
@@ -294,6 +328,24 @@ typedef struct {
 } tasft_scores_target_args;
 TASFT_API int64_t tasft_scores_target_workspace_size(int32_t B, int32_t H, int32_t Sq, int32_t Sk, int32_t block);
 TASFT_API int tasft_gate_target_from_scores(const tasft_scores_target_args* args, tasft_stream_t stream);
+
+/* Training forward in one pass: the attention output of tasft_bsa_prefill_fwd (pass kept
+ * lists with every causal block for the reference's dense training attention) and, from
+ * the same on-chip S tiles, the block maxima of the scores (the S x S score tensor is never
+ * formed) and their softmax target. Replaces TASFTAttention._training_forward's
+ * scores / softmax / P V (tasft/modules/tasft_attention.py:427-466) plus
+ * TASFTObjective.compute_gate_target (tasft/training/objectives.py:128-185). Only the
+ * tcgen05 shapes (bf16/fp16, block 64, D 64/128, padded layout); other shapes return
+ * TASFT_ERR_UNSUPPORTED (use tasft_bsa_prefill_fwd + tasft_gate_target_fwd). */
+typedef struct {
+  tasft_prefill_args base;
+  float* block_max;       /* out [B, Hq, NB, NB] fp32: max of (Q K^T) * scale per visited tile, -inf elsewhere */
+  float* target;          /* out [B, Hq, NB, NB] fp32 softmax over the grid, or NULL */
+  float temperature;      /* 1 = compute_gate_target; 2 = TASFTAttention._compute_gate_target */
+  float clamp;            /* <= 0: none; else clamp finite maxima to [-clamp, clamp] before the softmax */
+  int32_t emulate_bf16_scores; /* round the maxima as the reference's bf16 (Q K^T) * scale */
+} tasft_train_fwd_args;
+TASFT_API int tasft_attention_train_fwd(const tasft_train_fwd_args* args, tasft_stream_t stream);
 
 typedef struct {
   const float* soft;      /* [B, H, NB, NB] gate scores */

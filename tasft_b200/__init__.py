@@ -18,7 +18,15 @@ from tasft_b200.decode import DecodeWorkspace, bsa_decode, bsa_decode_paged, dec
 from tasft_b200.exceptions import KernelError, NaNDetectedError, TASFTError, ValidationError
 from tasft_b200.patch import patch, unpatch
 from tasft_b200 import shards
-from tasft_b200.training import TASFTObjective, gate_losses, gate_objective, gate_target_from_qk
+from tasft_b200.training import (
+    ObjectiveLossOutput,
+    TASFTObjective,
+    gate_losses,
+    gate_objective,
+    gate_target_from_qk,
+    gate_target_from_scores,
+    training_attention,
+)
 from tasft_b200.types import VALID_BLOCK_SIZES, KeptBlocks
 
 __all__ = [
@@ -31,6 +39,7 @@ __all__ = [
     "KernelBackend",
     "KernelError",
     "NaNDetectedError",
+    "ObjectiveLossOutput",
     "SparsityStats",
     "TASFTError",
     "TASFTObjective",
@@ -42,9 +51,11 @@ __all__ = [
     "gate_losses",
     "gate_objective",
     "gate_target_from_qk",
+    "gate_target_from_scores",
     "mask_to_kept",
     "patch",
     "shards",
     "threshold_scores",
+    "training_attention",
     "unpatch",
 ]

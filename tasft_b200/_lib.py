@@ -68,6 +68,13 @@ class PrefillArgs(C.Structure):
     ]
 
 
+class TrainFwdArgs(C.Structure):
+    _fields_ = [
+        ("base", PrefillArgs), ("block_max", vp), ("target", vp), ("temperature", C.c_float), ("clamp", C.c_float),
+        ("emulate_bf16_scores", C.c_int32),
+    ]
+
+
 class PrefillVarlenArgs(C.Structure):
     _fields_ = [("base", PrefillArgs), ("cu_seqlens", vp), ("total", C.c_int32)]
 
@@ -94,6 +101,14 @@ class CombineArgs(C.Structure):
     _fields_ = [
         ("part_o", vp), ("part_ml", vp), ("G", C.c_int32), ("rows", C.c_int64), ("D", C.c_int32),
         ("out", vp), ("dtype", C.c_int32),
+    ]
+
+
+class PeerCombineArgs(C.Structure):
+    _fields_ = [
+        ("part_o", vp), ("part_ml", vp), ("rows", C.c_int64), ("D", C.c_int32), ("world", C.c_int32),
+        ("rank", C.c_int32), ("mailboxes", vp), ("epoch", vp), ("out", vp), ("dtype", C.c_int32),
+        ("timeout_ns", C.c_uint64), ("err", vp),
     ]
 
 
@@ -143,12 +158,20 @@ SIGNATURES = {
     "tasft_mask_to_kept": ([C.POINTER(MaskArgs), vp], C.c_int),
     "tasft_bsa_prefill_fwd": ([C.POINTER(PrefillArgs), vp], C.c_int),
     "tasft_bsa_prefill_varlen_fwd": ([C.POINTER(PrefillVarlenArgs), vp], C.c_int),
+    "tasft_attention_train_fwd": ([C.POINTER(TrainFwdArgs), vp], C.c_int),
     "tasft_decode_workspace_size": ([C.c_int32] * 5, C.c_int64),
     "tasft_bsa_decode_fwd": ([C.POINTER(DecodeArgs), vp], C.c_int),
     "tasft_bsa_decode_combine": ([C.POINTER(CombineArgs), vp], C.c_int),
     "tasft_bsa_decode_fwd_noalloc": ([C.POINTER(DecodeArgs), vp], C.c_int),
     "tasft_bsa_decode_paged_fwd": ([C.POINTER(PagedDecodeArgs), vp], C.c_int),
     "tasft_decode_noalloc_capacity": ([], C.c_int64),
+    "tasft_peer_mailbox_bytes": ([C.c_int32, C.c_int64, C.c_int32], C.c_int64),
+    "tasft_peer_alloc": ([C.c_int64, C.POINTER(vp)], C.c_int),
+    "tasft_peer_free": ([vp], C.c_int),
+    "tasft_ipc_handle": ([vp, C.c_char_p], C.c_int),
+    "tasft_ipc_open": ([C.c_char_p, C.POINTER(vp)], C.c_int),
+    "tasft_ipc_close": ([vp], C.c_int),
+    "tasft_peer_combine": ([C.POINTER(PeerCombineArgs), vp], C.c_int),
     "tasft_gate_target_workspace_size": ([C.c_int32] * 4, C.c_int64),
     "tasft_gate_target_fwd": ([C.POINTER(TargetArgs), vp], C.c_int),
     "tasft_scores_target_workspace_size": ([C.c_int32] * 5, C.c_int64),

@@ -24,7 +24,8 @@ void debug_log(const char* fmt, ...) {
 int prefill_simt(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu = nullptr);
 // Returns TASFT_ERR_UNSUPPORTED when the tcgen05 kernel does not cover the shape.
 // `cu` (cu_seqlens, B + 1 entries) and `total` describe packed sequences; nullptr / 0 otherwise.
-int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu = nullptr, int total = 0);
+int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu = nullptr, int total = 0,
+               float* bmax = nullptr, int emulate_bf16 = 0);
 }  // namespace tasft
 
 using namespace tasft;

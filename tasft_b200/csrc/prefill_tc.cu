@@ -155,7 +155,7 @@ template <int D, bool kF16>
 __global__ void __launch_bounds__(kThreads, 2)
     bsa_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv, const tasft_prefill_args a, const int NB,
-                          const int32_t* cu) {
+                          const int32_t* cu, float* bmax, const int emulate_bf16) {
   using L = Smem<D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -458,6 +458,20 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int qd = 0; qd < 4; ++qd) mq[qd] = max3(mq[qd], sv[c + 2 * qd], sv[c + 2 * qd + 1]);
         }
         const float mb = max3(mq[0], mq[1], fmaxf(mq[2], mq[3]));
+        if (bmax) {
+          // training-forward gate target: max of this 64 x 64 tile's scores (masked entries are
+          // -inf, as in the reference's triu(-inf) scores); rows of a slot span two warps, whose
+          // maxima meet in a float atomic max. Rounded as the reference's bf16 (Q K^T) * scale
+          // when asked (monotone rounding commutes with max).
+          float wm = warp_max(qpos < w.len ? mb : -INFINITY);  // padding rows past S do not count
+          if (lane == 0 && active && wm != -INFINITY) {
+            wm = emulate_bf16 ? __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(wm)) * a.scale))
+                              : wm * a.scale;
+            float* dst = bmax + (((int64_t)w.b * a.Hq + w.head[slot]) * NB + w.qbs[slot]) * NB + kb;
+            if (wm >= 0.f) atomicMax(reinterpret_cast<int*>(dst), __float_as_int(wm));
+            else atomicMin(reinterpret_cast<unsigned*>(dst), __float_as_uint(wm));
+          }
+        }
         const float m_new = fmaxf(m, mb * sl2);
         const bool need = (m != -INFINITY) && (m_new > m + kRescaleThreshold);
         if (m == -INFINITY) m = m_new;  // O row is still exactly zero: no rescale
@@ -551,7 +565,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 template <int D, bool kF16>
-int launch_tc(const tasft_prefill_args& a, const int32_t* cu, int total, cudaStream_t st) {
+int launch_tc(const tasft_prefill_args& a, const int32_t* cu, int total, cudaStream_t st, float* bmax,
+              int emulate_bf16) {
   const int es = 2;
   const int NB = (a.S + kBlk - 1) / kBlk;
   // packed sequences: one [1, H, total, D] tensor, rows offset by cu_seqlens in the kernel
@@ -579,14 +594,15 @@ int launch_tc(const tasft_prefill_args& a, const int32_t* cu, int total, cudaStr
   }
   if (grid > tiles) grid = tiles;
   if (debug_enabled()) debug_log("prefill_tc D=%d tiles=%lld grid=%lld smem=%d", D, (long long)tiles, (long long)grid, smem);
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB, cu);
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB, cu, bmax, emulate_bf16);
   count_launch();
   return launch_status();
 }
 
 }  // namespace
 
-int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu, int total) {
+int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu, int total, float* bmax,
+               int emulate_bf16) {
   if (a.block != kBlk) return TASFT_ERR_UNSUPPORTED;
   if (a.dtype != TASFT_BF16 && a.dtype != TASFT_F16) return TASFT_ERR_UNSUPPORTED;
   if (a.D != 64 && a.D != 128) return TASFT_ERR_UNSUPPORTED;
@@ -596,8 +612,12 @@ int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu, 
   if (!aligned16(a.out) || (a.o_stride[0] % 8) || (a.o_stride[1] % 8) || (a.o_stride[2] % 8))
     return TASFT_ERR_UNSUPPORTED;
   const bool f16 = a.dtype == TASFT_F16;
-  if (a.D == 128) return f16 ? launch_tc<128, true>(a, cu, total, st) : launch_tc<128, false>(a, cu, total, st);
-  return f16 ? launch_tc<64, true>(a, cu, total, st) : launch_tc<64, false>(a, cu, total, st);
+  if (bmax && cu) return TASFT_ERR_UNSUPPORTED;  // block maxima only for the padded layout
+  if (a.D == 128)
+    return f16 ? launch_tc<128, true>(a, cu, total, st, bmax, emulate_bf16)
+               : launch_tc<128, false>(a, cu, total, st, bmax, emulate_bf16);
+  return f16 ? launch_tc<64, true>(a, cu, total, st, bmax, emulate_bf16)
+             : launch_tc<64, false>(a, cu, total, st, bmax, emulate_bf16);
 }
 
 }  // namespace tasft

@@ -5,11 +5,19 @@
 //   (objectives.py:170-178), softmax over the flattened NB x NB grid (:180-185),
 //   KL(target || soft / sum soft) batchmean (:187-221), (mean(soft) - tau)^2 (:223-241).
 // Here the S x S score matrix is never stored: each tile's max is reduced on chip.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace tasft {
 
 int gate_target_blockmax_tc(const tasft_target_args& a, float* block_max, cudaStream_t st);
+int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu, int total, float* bmax,
+               int emulate_bf16);
+
+__global__ void fill_kernel(float* p, int64_t n, float v) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) p[i] = v;
+}
 
 // ---------------------------------------------------------------------------
 // CUDA-core tile max: one CTA per (q-block, k-block <= q-block, b*h).
@@ -536,6 +544,36 @@ extern "C" int tasft_gate_target_from_scores(const tasft_scores_target_args* ap,
   target_softmax_kernel<<<a.B * a.H, 512, 0, st>>>(bm, a.target, (int64_t)NBq * NBk, inv_t, a.clamp);
   count_launch();
   return launch_status();
+}
+
+// Training forward: attention (through the tcgen05 prefill kernel, which is dense when the
+// lists hold every causal block) and, from the same S tiles, the gate target's block maxima
+// and softmax. Replaces TASFTAttention._training_forward's score matrix + softmax + P V
+// (tasft/modules/tasft_attention.py:427-466) followed by compute_gate_target.
+extern "C" int tasft_attention_train_fwd(const tasft_train_fwd_args* ap, tasft_stream_t stream) {
+  if (!ap || !ap->block_max) return TASFT_ERR_INVALID_ARG;
+  const tasft_prefill_args& a = ap->base;
+  if (!a.q || !a.k || !a.v || !a.out || !a.kept_idx || !a.kept_cnt) return TASFT_ERR_INVALID_ARG;
+  if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.S <= 0 || a.D <= 0 || a.Hm <= 0 || a.Hq % a.Hk || a.Hq % a.Hm)
+    return TASFT_ERR_INVALID_ARG;
+  if (a.q_stride[3] != 1 || a.k_stride[3] != 1 || a.v_stride[3] != 1 || a.o_stride[3] != 1)
+    return TASFT_ERR_INVALID_ARG;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int NB = ceil_div(a.S, a.block);
+  const int64_t n = (int64_t)a.B * a.Hq * NB * NB;
+  fill_kernel<<<(unsigned)std::min<int64_t>(ceil_div(n, 256), 4096), 256, 0, st>>>(ap->block_max, n, -INFINITY);
+  count_launch();
+  int rc = launch_status();
+  if (rc != TASFT_OK) return rc;
+  rc = prefill_tc(a, st, nullptr, 0, ap->block_max, ap->emulate_bf16_scores);
+  if (rc != TASFT_OK) return rc;  // TASFT_ERR_UNSUPPORTED: not a tcgen05 shape
+  if (ap->target) {
+    const float inv_t = ap->temperature > 0.f ? 1.0f / ap->temperature : 1.0f;
+    target_softmax_kernel<<<a.B * a.Hq, 512, 0, st>>>(ap->block_max, ap->target, (int64_t)NB * NB, inv_t, ap->clamp);
+    count_launch();
+    rc = launch_status();
+  }
+  return rc;
 }
 
 extern "C" int64_t tasft_gate_loss_workspace_size(int32_t B, int32_t H) {

@@ -182,20 +182,88 @@ def long_context_decode(
     return decode_combine(ao, am, q.dtype)
 
 
+class PeerExchange:
+    """Merge of split-KV decode partials across the ranks of ``group`` over peer memory
+    (``tasft_peer_combine``): each rank pushes its partial into every rank's mailbox through
+    CUDA IPC mappings and merges what its own mailbox holds. No NCCL call per step, so the
+    step can be captured in a CUDA graph. Set up once (collective: every rank constructs it
+    in the same order); ``close()`` unmaps and frees."""
+
+    def __init__(self, rows: int, D: int, device, group=None, timeout_s: float = 1.0) -> None:
+        import ctypes as C  # noqa: PLC0415
+
+        import torch.distributed as dist  # noqa: PLC0415
+
+        from tasft_b200 import _lib as L  # noqa: PLC0415
+
+        self._L, self._C = L, C
+        lib = L.lib()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.D, self.device = rows, D, torch.device(device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        nbytes = int(lib.tasft_peer_mailbox_bytes(self.world, rows, D))
+        box = C.c_void_p()
+        L.check(lib.tasft_peer_alloc(nbytes, C.byref(box)), "tasft_peer_alloc")
+        self._own = box.value
+        h = C.create_string_buffer(64)
+        L.check(lib.tasft_ipc_handle(self._own, h), "tasft_ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h.raw), group=group)
+        self._opened = []
+        ptrs = []
+        for r, hr in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = C.c_void_p()
+            L.check(lib.tasft_ipc_open(C.c_char_p(hr), C.byref(p)), "tasft_ipc_open", peer=r)
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def __call__(self, part_o: torch.Tensor, part_ml: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        L = self._L
+        args = L.PeerCombineArgs(
+            part_o=part_o.data_ptr(), part_ml=part_ml.data_ptr(), rows=self.rows, D=self.D, world=self.world,
+            rank=self.rank, mailboxes=self.table.data_ptr(), epoch=self.epoch.data_ptr(), out=out.data_ptr(),
+            dtype=L.dtype_code(out), timeout_ns=self.timeout_ns, err=self.err.data_ptr(),
+        )
+        L.check(L.lib().tasft_peer_combine(args, L.stream_ptr(out.device)), "tasft_peer_combine")
+        return out
+
+    def close(self) -> None:
+        lib = self._L.lib()
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            lib.tasft_ipc_close(p)
+        self._opened = []
+        if self._own:
+            lib.tasft_peer_free(self._own)
+            self._own = None
+
+
 class SplitKVDecoder:
     """``long_context_decode`` with its buffers kept across calls (workspace, partials, the
     gather buffer), for a serving loop that decodes one token per step. ``local`` lets the
     caller pass the rank's rebased kept lists when they did not change since the last step."""
 
     def __init__(self, B: int, Hq: int, Hk: int, D: int, device, group=None, block: int = 64,
-                 num_splits: int = 0) -> None:
+                 num_splits: int = 0, exchange: str = "nccl", out_dtype=torch.bfloat16) -> None:
         import torch.distributed as dist  # noqa: PLC0415
 
         from tasft_b200.decode import DecodeWorkspace  # noqa: PLC0415
 
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange must be 'nccl' or 'peer', got {exchange!r}")
         self.group, self.block, self.num_splits = group, block, num_splits
         self.world = dist.get_world_size(group)
         self.nccl = dist.get_backend(group) == "nccl"
+        # "peer": partials merged over peer memory by one kernel (graph-capturable step)
+        self.peer = PeerExchange(B * Hq, D, device, group) if exchange == "peer" else None
+        self.out = torch.empty(B, Hq, D, dtype=out_dtype, device=device) if self.peer is not None else None
         self.ws = DecodeWorkspace(B, Hq, Hk, D, max(num_splits, 16), device)
         self.no, self.nm = B * Hq * D, B * Hq * 2
         self.flat = torch.empty(self.no + self.nm, dtype=torch.float32, device=device)
@@ -217,6 +285,8 @@ class SplitKVDecoder:
         kl = local if local is not None else local_kept(kept, block_lo, block_lo + nloc)
         bsa_decode(q, k_local, v_local, local_kv_len(kv_len, block_lo, block_lo + nloc, self.block), kl, self.block,
                    num_splits=self.num_splits, workspace=self.ws, partials=(self.po, self.pm))
+        if self.peer is not None:
+            return self.peer(self.po, self.pm, self.out)
         if self.nccl:
             dist.all_gather_into_tensor(self.gathered, self.flat, group=self.group)
         else:
@@ -228,4 +298,4 @@ class SplitKVDecoder:
 
 __all__ = ["assign_units", "block_range", "gather_partials", "local_kept", "local_kv_len", "long_context_decode",
            "prefill_units", "qblock_ranges", "restrict_qblocks", "scatter_units", "unit_slices", "unit_weights",
-           "SplitKVDecoder"]
+           "PeerExchange", "SplitKVDecoder"]

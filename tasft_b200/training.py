@@ -18,7 +18,7 @@ import torch
 import torch.nn.functional as F
 
 from tasft_b200 import _lib as L
-from tasft_b200.exceptions import NaNDetectedError
+from tasft_b200.exceptions import KernelError, NaNDetectedError
 
 
 def gate_target_from_qk(
@@ -211,6 +211,84 @@ def gate_target_from_scores(
     return (tgt, bm) if return_block_max else tgt
 
 
+def _train_fwd(q, k, v, block, temperature, clamp, emulate):
+    """Attention output + block maxima + target in one tcgen05 pass (dense causal lists);
+    for shapes that kernel does not take, the CUDA-core prefill and the target kernels."""
+    from tasft_b200.block_sparse_fa import BlockSparseFlashAttention, full_kept  # noqa: PLC0415
+
+    B, Hq, S, D = q.shape
+    Hk = k.shape[1]
+    nb = math.ceil(S / block)
+    kept = full_kept(B, Hk, nb, True, q.device)
+    out = torch.empty_like(q)
+    bm = torch.empty(B, Hq, nb, nb, dtype=torch.float32, device=q.device)
+    tgt = torch.empty_like(bm)
+    if block == 64 and q.dtype in (torch.bfloat16, torch.float16) and D in (64, 128):
+        base = L.PrefillArgs(
+            q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), out=out.data_ptr(), q_stride=L.strides4(q),
+            k_stride=L.strides4(k), v_stride=L.strides4(v), o_stride=L.strides4(out), B=B, Hq=Hq, Hk=Hk, S=S, D=D,
+            block=block, dtype=L.dtype_code(q), causal=1, scale=1.0 / math.sqrt(D), kept_idx=kept.idx.data_ptr(),
+            kept_cnt=kept.cnt.data_ptr(), Hm=Hk, err=None, force_simt=0,
+        )
+        args = L.TrainFwdArgs(base=base, block_max=bm.data_ptr(), target=tgt.data_ptr(), temperature=float(temperature),
+                              clamp=float(clamp) if clamp is not None else 0.0, emulate_bf16_scores=int(emulate))
+        rc = L.lib().tasft_attention_train_fwd(args, L.stream_ptr(q.device))
+        if rc == 0:
+            return out, tgt, bm
+        if rc != -2:
+            L.check(rc, "tasft_attention_train_fwd", shape=[B, Hq, Hk, S, D])
+    # other dtypes / blocks / head dims: the two kernels separately
+    out = BlockSparseFlashAttention(block_size=block).forward(q, k, v, kept) if block in (32, 64, 128) else None
+    if out is None:
+        raise KernelError(f"training attention: unsupported block size {block}", context={"block": block})
+    tgt, bm = gate_target_from_qk(q, k, block, emulate_bf16_scores=emulate, temperature=temperature, clamp=clamp,
+                                  return_block_max=True)
+    return out, tgt, bm
+
+
+class _TrainAttnFn(torch.autograd.Function):
+    """Forward: this library's fused attention + gate-target pass. Backward: the gradient of
+    dense causal attention w.r.t. q, k, v, recomputed by PyTorch's scaled_dot_product_attention
+    (the reference's training path differentiates its dense matmul/softmax the same way;
+    the target is a detached distillation signal, tasft_attention.py:446-453)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, block, temperature, clamp, emulate):
+        out, tgt, bm = _train_fwd(q, k, v, block, temperature, clamp, emulate)
+        ctx.save_for_backward(q, k, v)
+        ctx.mark_non_differentiable(tgt, bm)
+        return out, tgt, bm
+
+    @staticmethod
+    def backward(ctx, g_out, _g_tgt, _g_bm):
+        q, k, v = ctx.saved_tensors
+        with torch.enable_grad():
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+            o = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, enable_gqa=q.shape[1] != k.shape[1])
+            dq, dk, dv = torch.autograd.grad(o, (qq, kk, vv), g_out)
+        return dq, dk, dv, None, None, None, None
+
+
+def training_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block: int = 64, *,
+                       temperature: float = 1.0, clamp: float | None = None,
+                       emulate_bf16_scores: bool | None = None, return_block_max: bool = False):
+    """Dense causal attention for the training forward together with the gate target.
+
+    The reference forms the ``[B, H, S, S]`` scores, softmaxes them for the output and keeps
+    them for ``compute_gate_target`` (``tasft/modules/tasft_attention.py:427-466``,
+    ``tasft/training/objectives.py:128-185``). Here one kernel pass produces the output and the
+    per-tile score maxima (``tasft_attention_train_fwd``); the score tensor never exists.
+    K/V may have fewer heads (GQA). Returns ``(out, target)`` (and the block maxima when
+    asked); ``out`` is differentiable in q, k, v.
+    """
+    L.require_cuda(q, k, v)
+    if emulate_bf16_scores is None:
+        emulate_bf16_scores = q.dtype == torch.bfloat16
+    out, tgt, bm = _TrainAttnFn.apply(q.contiguous(), k.contiguous(), v.contiguous(), block, temperature, clamp,
+                                      bool(emulate_bf16_scores))
+    return (out, tgt, bm) if return_block_max else (out, tgt)
+
+
 def _check_finite(t: torch.Tensor, name: str, context: dict | None = None) -> None:
     if not torch.isfinite(t).all():
         has_nan = bool(torch.isnan(t).any())
@@ -343,4 +421,4 @@ class TASFTObjective:
 
 
 __all__ = ["ObjectiveLossOutput", "TASFTObjective", "gate_backward", "gate_losses", "gate_objective",
-           "gate_target_from_qk", "gate_target_from_scores"]
+           "gate_target_from_qk", "gate_target_from_scores", "training_attention"]
