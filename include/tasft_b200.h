@@ -20,6 +20,8 @@
  *   tasft_gate_mask_build      AttnGate.forward           tasft/modules/attn_gate.py:377-485
  *   tasft_mask_from_scores     soft >= tau (+ tril)       tasft/modules/attn_gate.py:466-477
  *   tasft_mask_to_kept         bool mask & block tril     tasft/kernels/block_sparse_fa.py:497-508
+ *   tasft_calibrate_tau        the weight-norm estimate of per-layer sparsity
+ *                                                         tasft/bundle/export.py:327-360
  *   tasft_bsa_prefill_fwd      _block_sparse_attn_fwd_kernel launch
  *                                                         tasft/kernels/block_sparse_fa.py:454-552
  *   tasft_bsa_decode_fwd       (none: new capability; the reference delegates decode
@@ -123,6 +125,19 @@ typedef struct {
   int32_t* num_kept;      /* out scalar or NULL */
 } tasft_threshold_args;
 TASFT_API int tasft_mask_from_scores(const tasft_threshold_args* args, tasft_stream_t stream);
+
+/* Threshold calibration: tau = the keep-th largest of n gate scores (exact radix select),
+ * so that `soft >= tau` keeps `keep` blocks (more only on ties at tau). Replaces the
+ * weight-norm sparsity estimate of tasft/bundle/export.py:327-360 with a measured per-layer
+ * tau. keep <= 0 gives +inf (keep nothing), keep > n gives -inf (keep everything). */
+typedef struct {
+  const float* scores;    /* [n] fp32 gate scores (the full grid, causal zeros included) */
+  int64_t n;
+  int64_t keep;
+  float* tau;             /* out device scalar */
+  int64_t* kept;          /* out device scalar: count of scores >= tau, or NULL */
+} tasft_calib_args;
+TASFT_API int tasft_calibrate_tau(const tasft_calib_args* args, tasft_stream_t stream);
 
 /* Bool block mask -> ascending kept lists (the reference kernel's visiting order). */
 typedef struct {

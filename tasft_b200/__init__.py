@@ -6,7 +6,7 @@ Drop-in replacements for the reference's hot-path API:
 plus a block-sparse decode and its split-KV combine. Compute runs in
 ``libtasft_b200.so`` (hand-written CUDA, C ABI in ``include/tasft_b200.h``).
 """
-from tasft_b200.attn_gate import AttnGate, GateOutput, threshold_scores
+from tasft_b200.attn_gate import AttnGate, GateOutput, calibrate_tau, measured_sparsity_profile, threshold_scores
 from tasft_b200.block_sparse_fa import (
     BlockSparseFlashAttention,
     KernelBackend,
@@ -45,6 +45,7 @@ __all__ = [
     "TASFTObjective",
     "ValidationError",
     "bsa_decode",
+    "calibrate_tau",
     "bsa_decode_paged",
     "decode_combine",
     "detect_kernels",
@@ -53,6 +54,7 @@ __all__ = [
     "gate_target_from_qk",
     "gate_target_from_scores",
     "mask_to_kept",
+    "measured_sparsity_profile",
     "patch",
     "shards",
     "threshold_scores",

@@ -51,6 +51,10 @@ class ThresholdArgs(C.Structure):
     ]
 
 
+class CalibArgs(C.Structure):
+    _fields_ = [("scores", vp), ("n", C.c_int64), ("keep", C.c_int64), ("tau", vp), ("kept", vp)]
+
+
 class MaskArgs(C.Structure):
     _fields_ = [
         ("mask", vp), ("rows", C.c_int64), ("NBq", C.c_int32), ("NBk", C.c_int32), ("causal", C.c_int32),
@@ -156,6 +160,7 @@ SIGNATURES = {
     "tasft_gate_mask_build": ([C.POINTER(GateArgs), vp], C.c_int),
     "tasft_mask_from_scores": ([C.POINTER(ThresholdArgs), vp], C.c_int),
     "tasft_mask_to_kept": ([C.POINTER(MaskArgs), vp], C.c_int),
+    "tasft_calibrate_tau": ([C.POINTER(CalibArgs), vp], C.c_int),
     "tasft_bsa_prefill_fwd": ([C.POINTER(PrefillArgs), vp], C.c_int),
     "tasft_bsa_prefill_varlen_fwd": ([C.POINTER(PrefillVarlenArgs), vp], C.c_int),
     "tasft_attention_train_fwd": ([C.POINTER(TrainFwdArgs), vp], C.c_int),

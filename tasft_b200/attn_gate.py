@@ -34,6 +34,14 @@ class GateOutput:
     _ratio: list = field(default_factory=list, repr=False)
 
     @property
+    def sparsity_ratio_device(self) -> torch.Tensor:
+        """``1 - mean(hard_mask)`` as a device scalar (fp32): no host synchronisation, for
+        callers that branch on the device or log asynchronously."""
+        total = self.hard_mask.numel()
+        kept = self._num_kept if self._num_kept is not None else self.hard_mask.sum()
+        return 1.0 - kept.reshape(()).float() / max(total, 1)
+
+    @property
     def sparsity_ratio(self) -> float:
         """``1 - mean(hard_mask)`` over the full grid (host sync on first access)."""
         if not self._ratio:
@@ -220,4 +228,44 @@ def threshold_scores(soft: torch.Tensor, tau: float, causal: bool) -> tuple[torc
     return hard, KeptBlocks(idx, cnt), num
 
 
-__all__ = ["AttnGate", "GateOutput", "threshold_scores"]
+def calibrate_tau(soft_scores: torch.Tensor, target_sparsity: float, *, sync: bool = True):
+    """Threshold that keeps ``round((1 - target_sparsity) * numel)`` of the given gate scores.
+
+    Measured replacement for the reference bundle's weight-norm sparsity estimate
+    (``tasft/bundle/export.py:327-360``): run the gate on calibration inputs, pass its
+    ``soft_scores`` (the full grid: causal zeros count, as in the reference's
+    ``sparsity_ratio``, ``attn_gate.py:477``), get the layer's tau. Exact (a radix select on
+    the device, ``tasft_calibrate_tau``); ties at tau are kept, so the achieved sparsity can
+    only be lower. Returns ``(tau, achieved_sparsity)`` as floats (one host sync), or as
+    device scalars with ``sync=False``.
+    """
+    L.require_cuda(soft_scores)
+    if not 0.0 <= target_sparsity <= 1.0:
+        raise ValidationError(f"target_sparsity must be in [0, 1], got {target_sparsity}",
+                              context={"target_sparsity": target_sparsity})
+    s = soft_scores.detach().float().contiguous().view(-1)
+    n = s.numel()
+    keep = int(round((1.0 - target_sparsity) * n))
+    tau = torch.empty((), dtype=torch.float32, device=s.device)
+    kept = torch.empty((), dtype=torch.int64, device=s.device)
+    args = L.CalibArgs(scores=s.data_ptr(), n=n, keep=keep, tau=tau.data_ptr(), kept=kept.data_ptr())
+    L.check(L.lib().tasft_calibrate_tau(args, L.stream_ptr(s.device)), "tasft_calibrate_tau")
+    achieved = 1.0 - kept.double() / n
+    if not sync:
+        return tau, achieved
+    return float(tau.item()), float(achieved.item())
+
+
+def measured_sparsity_profile(gates: dict, calib_qk: dict, target_sparsity: float) -> dict:
+    """Per-layer ``(tau, achieved_sparsity)`` measured on calibration Q/K, in the shape of the
+    reference exporter's ``_compute_sparsity_profile`` (``tasft/bundle/export.py:327-360``):
+    ``gates[i]`` an ``AttnGate``, ``calib_qk[i] = (q, k)`` that layer's inputs."""
+    out = {}
+    with torch.no_grad():
+        for i in sorted(gates):
+            q, k = calib_qk[i]
+            out[i] = calibrate_tau(gates[i](q, k).soft_scores, target_sparsity)
+    return out
+
+
+__all__ = ["AttnGate", "GateOutput", "calibrate_tau", "measured_sparsity_profile", "threshold_scores"]

@@ -276,6 +276,13 @@ class BlockSparseFlashAttention:
         return SparsityStats(total, active, ratio, self.estimate_speedup(ratio))
 
     @staticmethod
+    def sparsity_stats_device(block_mask: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """``(active_blocks, sparsity_ratio)`` as device scalars: the statistics of
+        :meth:`compute_sparsity_stats` without its host synchronisation."""
+        active = block_mask.sum()
+        return active, 1.0 - active.float() / max(block_mask.numel(), 1)
+
+    @staticmethod
     def estimate_speedup(sparsity_ratio: float) -> float:
         """The reference's model ``1 / (1 - s (1 - 0.02))`` (block_sparse_fa.py:597-618)."""
         return 1.0 / max(1e-6, 1.0 - sparsity_ratio * (1.0 - 0.02))

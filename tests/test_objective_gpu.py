@@ -182,3 +182,25 @@ def test_tensor_core_gate_target_d128_against_oracle():
     got2 = T.gate_target_from_qk(q.to(DEV), k.to(DEV), 64, temperature=2.0, clamp=50.0)
     ref2 = O.gate_target_from_qk(q, k, 64, temperature=2.0, clamp=50.0)
     assert (got2.cpu() - ref2.float()).abs().max().item() <= BF16_ATOL
+
+
+@pytest.mark.parametrize("target", [0.0, 0.5, 0.8, 0.93, 1.0])
+def test_calibrate_tau_exact_quantile(target):
+    g = torch.Generator().manual_seed(int(target * 100))
+    soft = torch.rand(2, 8, 64, 64, generator=g)
+    soft = soft * torch.ones(64, 64).tril()  # causal zeros count, as in the reference's sparsity
+    soft[0, 0, 5, :3] = 0.5  # ties
+    tau, achieved = T.calibrate_tau(soft.to(DEV), target)
+    n = soft.numel()
+    keep = int(round((1 - target) * n))
+    if keep == 0:
+        assert tau == float("inf") and achieved == 1.0
+        return
+    ref_tau = torch.sort(soft.view(-1), descending=True).values[keep - 1].item()
+    assert tau == ref_tau
+    assert achieved == pytest.approx(1.0 - (soft >= ref_tau).sum().item() / n)
+    assert achieved <= target + 1e-12
+    # the gate output's own sparsity as a device scalar, without a host sync
+    gate = T.AttnGate(4, 64).to(DEV)
+    out = gate(torch.randn(1, 4, 256, 64, device=DEV), torch.randn(1, 4, 256, 64, device=DEV))
+    assert abs(out.sparsity_ratio_device.item() - out.sparsity_ratio) <= 1e-6
