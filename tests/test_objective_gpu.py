@@ -199,7 +199,7 @@ def test_calibrate_tau_exact_quantile(target):
     ref_tau = torch.sort(soft.view(-1), descending=True).values[keep - 1].item()
     assert tau == ref_tau
     assert achieved == pytest.approx(1.0 - (soft >= ref_tau).sum().item() / n)
-    assert achieved <= target + 1e-12
+    assert achieved <= 1.0 - keep / n + 1e-12  # ties only ever keep more
     # the gate output's own sparsity as a device scalar, without a host sync
     gate = T.AttnGate(4, 64).to(DEV)
     out = gate(torch.randn(1, 4, 256, 64, device=DEV), torch.randn(1, 4, 256, 64, device=DEV))
