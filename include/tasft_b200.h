@@ -19,6 +19,8 @@
  * Reference interfaces replaced (v-code01/tasft, paths inside that project):
  *   tasft_gate_mask_build      AttnGate.forward           tasft/modules/attn_gate.py:377-485
  *   tasft_mask_from_scores     soft >= tau (+ tril)       tasft/modules/attn_gate.py:466-477
+ *   tasft_qkv_rope_pool        _prepare_qkv head split + rotary + the gate's pooling
+ *                              tasft/modules/tasft_attention.py:615-742, attn_gate.py:351-375
  *   tasft_mask_to_kept         bool mask & block tril     tasft/kernels/block_sparse_fa.py:497-508
  *   tasft_calibrate_tau        the weight-norm estimate of per-layer sparsity
  *                                                         tasft/bundle/export.py:327-360
@@ -108,7 +110,36 @@ typedef struct {
  * (ABI 2 added `D`). */
 TASFT_API int64_t tasft_gate_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t Sq, int32_t Sk,
                                   int32_t block, int32_t hidden, int32_t D);
+/* Pooled-input mode: with q == k == NULL, pooled_q / pooled_k are INPUTS (the block means
+ * from tasft_qkv_rope_pool) and the pooling pass is skipped; hidden 32 or 64, D % 4 == 0. */
 TASFT_API int tasft_gate_mask_build(const tasft_gate_args* args, tasft_stream_t stream);
+
+/* Q/K/V projection epilogue: head split [B, S, H*D] -> [B, H, S, D], rotary embedding of
+ * Q and K (x * cos + rotate_half(x) * sin, each op rounded to the dtype as the reference's
+ * element-wise ops are), and the fp32 block means of the rotated Q and K that AttnGate pools
+ * (zero padding counts). Replaces TASFTAttention._prepare_qkv's view / transpose / rotary
+ * (tasft/modules/tasft_attention.py:615-742, :872-908) and the gate's pooling pass
+ * (tasft/modules/attn_gate.py:351-375); K/V are not repeated per q-head. Pass the means
+ * to tasft_gate_mask_build with q = k = NULL (pooled-input mode). */
+typedef struct {
+  const void* q_in;       /* [B, S, Hq*D] rows; element strides (batch, token) below, D contiguous */
+  const void* k_in;       /* [B, S, Hk*D] */
+  const void* v_in;       /* [B, S, Hk*D] */
+  int64_t q_in_stride[2], k_in_stride[2], v_in_stride[2];
+  const void* cos;        /* [B or 1, S, D] (HF layout, halves duplicated); unused when rope == 0 */
+  const void* sin;
+  int64_t cs_stride[2];   /* batch stride (0 = shared over the batch), token stride */
+  void* q_out;            /* [B, Hq, S, D] contiguous */
+  void* k_out;            /* [B, Hk, S, D] contiguous */
+  void* v_out;            /* [B, Hk, S, D] contiguous */
+  float* pooled_q;        /* out [B, Hq, NB, D] fp32 block means of the rotated Q, or NULL */
+  float* pooled_k;        /* out [B, Hk, NB, D], or NULL */
+  int32_t B, Hq, Hk, S, D;
+  int32_t block;          /* gate block size (tokens) */
+  int32_t dtype;
+  int32_t rope;           /* 1 = apply the rotary embedding to Q and K, 0 = layout only */
+} tasft_qkv_args;
+TASFT_API int tasft_qkv_rope_pool(const tasft_qkv_args* args, tasft_stream_t stream);
 
 /* Threshold given fp32 scores: hard = (soft >= tau) (& block tril when causal),
  * ascending kept lists, counts and the total. Bit-exact with the reference's

@@ -25,6 +25,7 @@ import torch.nn.functional as F
 
 __all__ = [
     "pool_to_blocks",
+    "apply_rotary",
     "gate_forward",
     "gate_forward_gqa",
     "kept_from_mask",
@@ -342,6 +343,18 @@ def decode_combine(o_parts, m_parts, l_parts):
 # ---------------------------------------------------------------------------
 # Gate target and losses (tasft/training/objectives.py)
 # ---------------------------------------------------------------------------
+
+
+def apply_rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotary embedding as ``_apply_rotary_pos_emb`` applies it
+    (``tasft/modules/tasft_attention.py:872-908``): ``x * cos + rotate_half(x) * sin`` with
+    ``rotate_half(x) = cat(-x[..., D/2:], x[..., :D/2])``, element-wise in ``x``'s dtype;
+    ``cos`` / ``sin`` ``[B, S, D]`` gain a head axis."""
+    if cos.ndim == 3:
+        cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return (x * cos) + (rot * sin)
 
 
 def training_scores(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:

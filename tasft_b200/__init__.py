@@ -6,7 +6,14 @@ Drop-in replacements for the reference's hot-path API:
 plus a block-sparse decode and its split-KV combine. Compute runs in
 ``libtasft_b200.so`` (hand-written CUDA, C ABI in ``include/tasft_b200.h``).
 """
-from tasft_b200.attn_gate import AttnGate, GateOutput, calibrate_tau, measured_sparsity_profile, threshold_scores
+from tasft_b200.attn_gate import (
+    AttnGate,
+    GateOutput,
+    calibrate_tau,
+    measured_sparsity_profile,
+    qkv_rope_pool,
+    threshold_scores,
+)
 from tasft_b200.block_sparse_fa import (
     BlockSparseFlashAttention,
     KernelBackend,
@@ -56,6 +63,7 @@ __all__ = [
     "mask_to_kept",
     "measured_sparsity_profile",
     "patch",
+    "qkv_rope_pool",
     "shards",
     "threshold_scores",
     "training_attention",

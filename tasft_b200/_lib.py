@@ -44,6 +44,16 @@ class GateArgs(C.Structure):
     ]
 
 
+class QkvArgs(C.Structure):
+    _fields_ = [
+        ("q_in", vp), ("k_in", vp), ("v_in", vp), ("q_in_stride", C.c_int64 * 2), ("k_in_stride", C.c_int64 * 2),
+        ("v_in_stride", C.c_int64 * 2), ("cos", vp), ("sin", vp), ("cs_stride", C.c_int64 * 2),
+        ("q_out", vp), ("k_out", vp), ("v_out", vp), ("pooled_q", vp), ("pooled_k", vp),
+        ("B", C.c_int32), ("Hq", C.c_int32), ("Hk", C.c_int32), ("S", C.c_int32), ("D", C.c_int32),
+        ("block", C.c_int32), ("dtype", C.c_int32), ("rope", C.c_int32),
+    ]
+
+
 class ThresholdArgs(C.Structure):
     _fields_ = [
         ("soft", vp), ("rows", C.c_int64), ("NBq", C.c_int32), ("NBk", C.c_int32), ("causal", C.c_int32),
@@ -159,6 +169,7 @@ SIGNATURES = {
     "tasft_gate_workspace_size": ([C.c_int32] * 8, C.c_int64),
     "tasft_gate_mask_build": ([C.POINTER(GateArgs), vp], C.c_int),
     "tasft_mask_from_scores": ([C.POINTER(ThresholdArgs), vp], C.c_int),
+    "tasft_qkv_rope_pool": ([C.POINTER(QkvArgs), vp], C.c_int),
     "tasft_mask_to_kept": ([C.POINTER(MaskArgs), vp], C.c_int),
     "tasft_calibrate_tau": ([C.POINTER(CalibArgs), vp], C.c_int),
     "tasft_bsa_prefill_fwd": ([C.POINTER(PrefillArgs), vp], C.c_int),

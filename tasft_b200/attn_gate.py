@@ -10,6 +10,7 @@ sparsity ratio is read from the device lazily, on first access.
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 from dataclasses import dataclass, field
 
@@ -197,6 +198,49 @@ class AttnGate(nn.Module):
         return GateOutput(soft_scores=soft, hard_mask=hard, num_blocks_q=nbq, num_blocks_k=nbk,
                           kept=KeptBlocks(idx, cnt), _num_kept=num)
 
+    def forward_pooled(self, pooled_q: torch.Tensor, pooled_k: torch.Tensor, seq_q: int, seq_k: int,
+                       threshold: float | None = None) -> GateOutput:
+        """The gate from block means already computed by :func:`qkv_rope_pool`
+        (``pooled_q [B, Hq, NBq, D]``, ``pooled_k [B, Hk, NBk, D]`` fp32): the projection and
+        pair kernels only, no pass over Q and K. Inference only (no autograd)."""
+        tau = threshold if threshold is not None else self.default_threshold
+        L.require_cuda(pooled_q, pooled_k)
+        B, Hq, nbq, D = pooled_q.shape
+        Hk, nbk = pooled_k.shape[1], pooled_k.shape[2]
+        if Hq != self.num_heads or D != self.head_dim or Hq % Hk:
+            raise ValidationError("pooled means do not match the gate",
+                                  context={"pooled_q": list(pooled_q.shape), "pooled_k": list(pooled_k.shape)})
+        blk = self.block_size
+        if math.ceil(seq_q / blk) != nbq or math.ceil(seq_k / blk) != nbk:
+            raise ValidationError("sequence lengths do not match the pooled block counts",
+                                  context={"seq_q": seq_q, "seq_k": seq_k, "nbq": nbq, "nbk": nbk})
+        dev = pooled_q.device
+        pq = pooled_q.float().contiguous()
+        pk = pooled_k.float().contiguous()
+        hid = self.gate_hidden_dim
+        w_in = self.gate_proj_in.weight.detach().float().contiguous()
+        b_in = self.gate_proj_in.bias.detach().float().contiguous()
+        w_out = self.gate_proj_out.weight.detach().float().contiguous().view(-1)
+        soft = torch.empty(B, Hq, nbq, nbk, dtype=torch.float32, device=dev)
+        hard = torch.empty(B, Hq, nbq, nbk, dtype=torch.bool, device=dev)
+        idx = torch.empty(B, Hq, nbq, nbk, dtype=torch.int32, device=dev)
+        cnt = torch.empty(B, Hq, nbq, dtype=torch.int32, device=dev)
+        num = torch.zeros(1, dtype=torch.int32, device=dev)
+        lib = L.lib()
+        ws_bytes = lib.tasft_gate_workspace_size(B, Hq, Hk, seq_q, seq_k, blk, hid, D)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        args = L.GateArgs(
+            q=None, k=None, B=B, Hq=Hq, Hk=Hk, Sq=seq_q, Sk=seq_k, D=D, block=blk, dtype=L.F32, hidden=hid,
+            w_in=w_in.data_ptr(), b_in=b_in.data_ptr(), w_out=w_out.data_ptr(), causal=int(self.is_causal),
+            tau=float(tau), soft=soft.data_ptr(), hard=hard.data_ptr(), kept_idx=idx.data_ptr(),
+            kept_cnt=cnt.data_ptr(), num_kept=num.data_ptr(), pooled_q=pq.data_ptr(), pooled_k=pk.data_ptr(),
+            workspace=ws.data_ptr(), workspace_bytes=ws_bytes,
+        )
+        L.check(lib.tasft_gate_mask_build(args, L.stream_ptr(dev)), "tasft_gate_mask_build (pooled)",
+                shape=[B, Hq, Hk, nbq, nbk, D])
+        return GateOutput(soft_scores=soft, hard_mask=hard, num_blocks_q=nbq, num_blocks_k=nbk,
+                          kept=KeptBlocks(idx, cnt), _num_kept=num)
+
     def compute_sparsity(self, soft_scores: torch.Tensor, threshold: float) -> float:
         """``1 - mean(soft >= tau)`` (attn_gate.py:487-497)."""
         return 1.0 - (soft_scores >= threshold).float().mean().item()
@@ -226,6 +270,50 @@ def threshold_scores(soft: torch.Tensor, tau: float, causal: bool) -> tuple[torc
                            num_kept=num.data_ptr())
     L.check(L.lib().tasft_mask_from_scores(args, L.stream_ptr(s.device)), "tasft_mask_from_scores")
     return hard, KeptBlocks(idx, cnt), num
+
+
+def qkv_rope_pool(q_lin: torch.Tensor, k_lin: torch.Tensor, v_lin: torch.Tensor, num_heads: int,
+                  num_kv_heads: int, cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                  block: int = 64):
+    """Projection epilogue (``tasft_qkv_rope_pool``): ``[B, S, H*D]`` projection outputs ->
+    rotated ``q [B, Hq, S, D]``, ``k, v [B, Hk, S, D]`` and the fp32 block means of q and k
+    for :meth:`AttnGate.forward_pooled`, in one pass. ``cos`` / ``sin`` ``[B or 1, S, D]`` in
+    the model dtype as a HF rotary embedding returns them (None: no rotation). Follows
+    ``TASFTAttention._prepare_qkv`` (``tasft/modules/tasft_attention.py:615-742``) and
+    ``_apply_rotary_pos_emb`` (``:872-908``) without the per-q-head repeat of K/V."""
+    L.require_cuda(q_lin, k_lin, v_lin)
+    B, S, qd = q_lin.shape
+    D = qd // num_heads
+    if qd != num_heads * D or k_lin.shape != (B, S, num_kv_heads * D) or v_lin.shape != k_lin.shape:
+        raise ValidationError("projection shapes do not match the head counts",
+                              context={"q": list(q_lin.shape), "k": list(k_lin.shape), "v": list(v_lin.shape)})
+    dev, dt = q_lin.device, q_lin.dtype
+    qi, ki, vi = (x if x.stride(-1) == 1 else x.contiguous() for x in (q_lin, k_lin, v_lin))
+    nb = math.ceil(S / block)
+    q = torch.empty(B, num_heads, S, D, dtype=dt, device=dev)
+    k = torch.empty(B, num_kv_heads, S, D, dtype=dt, device=dev)
+    v = torch.empty_like(k)
+    pq = torch.empty(B, num_heads, nb, D, dtype=torch.float32, device=dev)
+    pk = torch.empty(B, num_kv_heads, nb, D, dtype=torch.float32, device=dev)
+    rope = cos is not None
+    if rope:
+        if cos.ndim == 2:
+            cos, sin = cos.unsqueeze(0), sin.unsqueeze(0)
+        cos = cos.to(dt).contiguous()
+        sin = sin.to(dt).contiguous()
+        cs_stride = (cos.stride(0) if cos.shape[0] == B and B > 1 else 0, cos.stride(1))
+    else:
+        cs_stride = (0, 0)
+    args = L.QkvArgs(
+        q_in=qi.data_ptr(), k_in=ki.data_ptr(), v_in=vi.data_ptr(), q_in_stride=(C.c_int64 * 2)(qi.stride(0), qi.stride(1)),
+        k_in_stride=(C.c_int64 * 2)(ki.stride(0), ki.stride(1)), v_in_stride=(C.c_int64 * 2)(vi.stride(0), vi.stride(1)),
+        cos=cos.data_ptr() if rope else None, sin=sin.data_ptr() if rope else None,
+        cs_stride=(C.c_int64 * 2)(*cs_stride), q_out=q.data_ptr(), k_out=k.data_ptr(), v_out=v.data_ptr(),
+        pooled_q=pq.data_ptr(), pooled_k=pk.data_ptr(), B=B, Hq=num_heads, Hk=num_kv_heads, S=S, D=D, block=block,
+        dtype=L.dtype_code(q_lin), rope=int(rope),
+    )
+    L.check(L.lib().tasft_qkv_rope_pool(args, L.stream_ptr(dev)), "tasft_qkv_rope_pool", shape=[B, S, num_heads, D])
+    return q, k, v, pq, pk
 
 
 def calibrate_tau(soft_scores: torch.Tensor, target_sparsity: float, *, sync: bool = True):
@@ -268,4 +356,5 @@ def measured_sparsity_profile(gates: dict, calib_qk: dict, target_sparsity: floa
     return out
 
 
-__all__ = ["AttnGate", "GateOutput", "calibrate_tau", "measured_sparsity_profile", "threshold_scores"]
+__all__ = ["AttnGate", "GateOutput", "calibrate_tau", "measured_sparsity_profile", "qkv_rope_pool",
+           "threshold_scores"]

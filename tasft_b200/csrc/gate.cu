@@ -621,14 +621,16 @@ static int launch_pool(const tasft_gate_args& a, float* A, float* Ct, float* mq,
 extern "C" int tasft_gate_mask_build(const tasft_gate_args* ap, tasft_stream_t stream) {
   if (!ap) return TASFT_ERR_INVALID_ARG;
   const tasft_gate_args& a = *ap;
-  if (!a.q || !a.k || !a.w_in || !a.b_in || !a.w_out || !a.soft) return TASFT_ERR_INVALID_ARG;
+  const bool pooled_in = !a.q && !a.k;  // block means given (tasft_qkv_rope_pool)
+  if (pooled_in && (!a.pooled_q || !a.pooled_k)) return TASFT_ERR_INVALID_ARG;
+  if ((!pooled_in && (!a.q || !a.k)) || !a.w_in || !a.b_in || !a.w_out || !a.soft) return TASFT_ERR_INVALID_ARG;
   if (a.B <= 0 || a.Hq <= 0 || a.Hk <= 0 || a.Sq <= 0 || a.Sk <= 0 || a.D <= 0 || a.block <= 0)
     return TASFT_ERR_INVALID_ARG;
   if (a.Hq % a.Hk != 0) return TASFT_ERR_INVALID_ARG;
   if (a.hidden <= 0 || a.hidden > 256) return TASFT_ERR_UNSUPPORTED;
   if (a.D > 1024) return TASFT_ERR_UNSUPPORTED;
   if ((a.kept_idx == nullptr) != (a.kept_cnt == nullptr)) return TASFT_ERR_INVALID_ARG;
-  if (a.q_stride[3] != 1 || a.k_stride[3] != 1) return TASFT_ERR_INVALID_ARG;
+  if (!pooled_in && (a.q_stride[3] != 1 || a.k_stride[3] != 1)) return TASFT_ERR_INVALID_ARG;
   const int64_t need = tasft_gate_workspace_size(a.B, a.Hq, a.Hk, a.Sq, a.Sk, a.block, a.hidden, a.D);
   if (!a.workspace || a.workspace_bytes < need) return TASFT_ERR_WORKSPACE;
   const int NBq = ceil_div(a.Sq, a.block), NBk = ceil_div(a.Sk, a.block);
@@ -640,7 +642,14 @@ extern "C" int tasft_gate_mask_build(const tasft_gate_args* ap, tasft_stream_t s
   float* mk = a.pooled_k ? a.pooled_k : means + (int64_t)a.B * a.Hq * NBq * a.D;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int rc;
-  switch (a.dtype) {
+  if (pooled_in) {
+    if ((a.hidden != 32 && a.hidden != 64) || a.D % 4 || !aligned16(mq) || !aligned16(mk))
+      return TASFT_ERR_UNSUPPORTED;
+    if (a.hidden == 32) launch_project<32>(a, mq, mk, A, Ct, NBq, NBk, st);
+    else launch_project<64>(a, mq, mk, A, Ct, NBq, NBk, st);
+    count_launch();
+    rc = launch_status();
+  } else switch (a.dtype) {
     case TASFT_F32: rc = launch_pool<float>(a, A, Ct, mq, mk, NBq, NBk, st); break;
     case TASFT_BF16: rc = launch_pool<__nv_bfloat16>(a, A, Ct, mq, mk, NBq, NBk, st); break;
     case TASFT_F16: rc = launch_pool<__half>(a, A, Ct, mq, mk, NBq, NBk, st); break;
