@@ -341,6 +341,44 @@ def bench_triton_ref(q, ke, ve, mask_q, ours_out, flops, ours_ms, flush, args):
         return {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
 
 
+def bench_epilogue_gate(gate, flush, ws, args, peaks):
+    """The inference flow with the projection epilogue (``qkv_rope_pool``: head split +
+    rotary + the gate's block means in one pass over the q/k/v projection outputs) and the
+    gate run from those means (``AttnGate.forward_pooled``): the gate no longer re-reads Q
+    and K. Algorithmic bytes of the epilogue: read + write of q, k, v (+ cos/sin)."""
+    import tasft_b200 as T  # noqa: PLC0415
+
+    c = CFG
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(77)
+    ql = torch.randn(c["B"], c["S"], c["Hq"] * c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    kl = torch.randn(c["B"], c["S"], c["Hk"] * c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+    vl = torch.randn_like(kl)
+    inv = 1.0 / (10000 ** (torch.arange(0, c["D"], 2, device=dev).float() / c["D"]))
+    ang = torch.outer(torch.arange(c["S"], device=dev).float(), inv)
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().bfloat16()[None], emb.sin().bfloat16()[None]
+    res = {}
+
+    def epi():
+        res["o"] = T.qkv_rope_pool(ql, kl, vl, c["Hq"], c["Hk"], cos, sin, c["block"])
+
+    t_e = time_steps(epi, args.steps, args.warmup, flush, ws)
+    ms_e = statistics.mean(t_e)
+    _, _, _, pq, pk = res["o"]
+    nbytes = 2 * (ql.numel() + kl.numel() + vl.numel()) * 2 + 2 * cos.numel() * 2
+    t_g = time_steps(graphed(lambda: gate.forward_pooled(pq, pk, c["S"], c["S"])), args.steps, args.warmup, flush, ws)
+    ms_g = statistics.mean(t_g)
+    return {"epilogue_ms": round(ms_e, 4),
+            "epilogue_roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_e * 1e-3) / 1e9, 1),
+                                  "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                  "frac": round(nbytes / (ms_e * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                                  "algorithmic": f"{nbytes / 1e6:.1f} MB (read + write of q, k, v; cos, sin)"},
+            "gate_from_means_ms": round(ms_g, 4),
+            "what": "qkv_rope_pool (tasft_qkv_rope_pool) on [B, S, H*D] projection outputs, then "
+                    "AttnGate.forward_pooled (projection + pair kernels, CUDA graph replay)"}
+
+
 def bench_gate_train(q, k, flush, ws, args):
     """BASELINE configs[4] end to end: gate forward (autograd), target from Q and K, KL +
     sparsity loss, backward to the gate parameters. Times the whole step and the
@@ -621,6 +659,9 @@ def run_ours(args):
                               "frac": round(gbytes / (ms_g * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                               "traffic": traffic.get("gate_pool"),
                               "algorithmic": f"{gbytes / 1e6:.1f} MB per step (|Q| + |K|)"}}
+
+    # ---------------- projection epilogue + gate from its block means ----------------
+    gate_info["pooled_path"] = bench_epilogue_gate(_gate, flush, ws, args, peaks)
 
     # ---------------- training gate target (tensor-core bound: causal Q K^T tiles) ----------------
     def tstep():

@@ -76,8 +76,10 @@ __global__ void __launch_bounds__(kQkvThreads) qkv_rope_pool_kernel(tasft_qkv_ar
         for (int e = 0; e < V; ++e) {
           const float a1 = to_f<T>(x1[e]), a2 = to_f<T>(x2[e]);
           // rotate_half(x) = [-x2, x1]
-          const float o1 = rnd<T>(rnd<T>(a1 * to_f<T>(c1[e])) + rnd<T>(-a2 * to_f<T>(s1[e])));
-          const float o2 = rnd<T>(rnd<T>(a2 * to_f<T>(c2[e])) + rnd<T>(a1 * to_f<T>(s2[e])));
+          // explicit _rn ops: no fused multiply-add, so each product is rounded like the
+          // reference's separate element-wise multiplications
+          const float o1 = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(a1, to_f<T>(c1[e]))), rnd<T>(__fmul_rn(-a2, to_f<T>(s1[e])))));
+          const float o2 = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(a2, to_f<T>(c2[e]))), rnd<T>(__fmul_rn(a1, to_f<T>(s2[e])))));
           x1[e] = from_f<T>(o1);
           x2[e] = from_f<T>(o2);
         }
