@@ -437,6 +437,8 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_kernel(tasft_gate_
 // group's q-heads read the same slab), one warp per row, lanes over k-blocks.
 constexpr int kSlabRowsDefault = 16;  // q-rows per CTA (4 per warp): the Ct slab staging is amortised
 
+// HID = hidden width when it is 32 or 64 (a_i and w_out then live in registers), 0 otherwise.
+template <int HID>
 __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_slab_kernel(tasft_gate_args a, const float* A,
                                                                           const float* Ct, int NBq, int NBk,
                                                                           int kSlabRows) {
@@ -479,18 +481,37 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_slab_kernel(tasft_
     const int64_t row = ((int64_t)b * a.Hq + hk * grp + lr / NBq) * NBq + i;
     const float* ar = arows + r * hid;
     int cnt = 0, kept_total = 0;
+    float arr[HID > 0 ? HID : 1];  // this row's a_i, and w_out, in registers (HID known)
+    float wr[HID > 0 ? HID : 1];
+    if constexpr (HID > 0) {
+#pragma unroll
+      for (int h = 0; h < HID; h += 4) {
+        const float4 av = *reinterpret_cast<const float4*>(ar + h);
+        const float4 wv = *reinterpret_cast<const float4*>(wout + h);
+        arr[h] = av.x; arr[h + 1] = av.y; arr[h + 2] = av.z; arr[h + 3] = av.w;
+        wr[h] = wv.x; wr[h + 1] = wv.y; wr[h + 2] = wv.z; wr[h + 3] = wv.w;
+      }
+    }
     for (int j0 = 0; j0 < NBk; j0 += 32) {
       const int j = j0 + lane;
       const bool in_range = j < NBk;
       float s = 0.f;
       if (in_range) {
         float l0 = 0.f, l1 = 0.f;
-        int h = 0;
-        for (; h + 1 < hid; h += 2) {
-          l0 = fmaf(wout[h], fmaxf(ar[h] + ct[h * NBk + j], 0.f), l0);
-          l1 = fmaf(wout[h + 1], fmaxf(ar[h + 1] + ct[(h + 1) * NBk + j], 0.f), l1);
+        if constexpr (HID > 0) {
+#pragma unroll
+          for (int h = 0; h < HID; h += 2) {
+            l0 = fmaf(wr[h], fmaxf(arr[h] + ct[h * NBk + j], 0.f), l0);
+            l1 = fmaf(wr[h + 1], fmaxf(arr[h + 1] + ct[(h + 1) * NBk + j], 0.f), l1);
+          }
+        } else {
+          int h = 0;
+          for (; h + 1 < hid; h += 2) {
+            l0 = fmaf(wout[h], fmaxf(ar[h] + ct[h * NBk + j], 0.f), l0);
+            l1 = fmaf(wout[h + 1], fmaxf(ar[h + 1] + ct[(h + 1) * NBk + j], 0.f), l1);
+          }
+          if (h < hid) l0 = fmaf(wout[h], fmaxf(ar[h] + ct[h * NBk + j], 0.f), l0);
         }
-        if (h < hid) l0 = fmaf(wout[h], fmaxf(ar[h] + ct[h * NBk + j], 0.f), l0);
         s = 1.0f / (1.0f + __expf(-(l0 + l1)));
         if (causal && j > i) s = 0.f;
         a.soft[row * NBk + j] = s;
@@ -660,7 +681,8 @@ extern "C" int tasft_gate_mask_build(const tasft_gate_args* ap, tasft_stream_t s
   if (const char* e = std::getenv("TASFT_GATE_SLAB_ROWS")) kSlabRows = std::max(1, std::atoi(e));  // tuning aid
   const size_t slab = (size_t)(a.hidden * NBk + kSlabRows * a.hidden + a.hidden) * sizeof(float);
   if (slab <= 96 * 1024) {
-    auto kern = gate_pair_slab_kernel;
+    auto kern = a.hidden == 32 ? gate_pair_slab_kernel<32> : a.hidden == 64 ? gate_pair_slab_kernel<64>
+                                                                                : gate_pair_slab_kernel<0>;
     if (slab > 48 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)slab) != cudaSuccess)
       return TASFT_ERR_CUDA;
