@@ -155,7 +155,7 @@ template <int D, bool kF16>
 __global__ void __launch_bounds__(kThreads, 2)
     bsa_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv, const tasft_prefill_args a, const int NB,
-                          const int32_t* cu, float* bmax, const int emulate_bf16) {
+                          const int32_t* cu, float* bmax, const int emulate_bf16, const int wait_pv) {
   using L = Smem<D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -361,7 +361,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       // S(gi) may overwrite S buffer gi & 1 once P.V of block gi - 2 has run
       auto ready_s = [&](int gi) -> bool {
         if (!mbar_wait(&k_full[gi & 1], (gi >> 1) & 1)) { where = 4; return false; }
-        if (gi >= 2 && !mbar_wait(&pv_done[gi & 1], ((gi - 2) >> 1) & 1)) { where = 5; return false; }
+        // S(gi) overwrites P(gi - 2) in TMEM. P.V(gi - 2) was issued earlier by this thread, and
+        // MMAs issued by one thread run through the tensor pipe in issue order (CUTLASS's sm100
+        // FMHA mainloop writes its next Q K^T over the P its last P V reads the same way), so
+        // no wait is needed; wait_pv restores the completion wait (a checking aid).
+        if (wait_pv && gi >= 2 && !mbar_wait(&pv_done[gi & 1], ((gi - 2) >> 1) & 1)) { where = 5; return false; }
         tc::tc_fence_after();
         return true;
       };
@@ -594,7 +598,8 @@ int launch_tc(const tasft_prefill_args& a, const int32_t* cu, int total, cudaStr
   }
   if (grid > tiles) grid = tiles;
   if (debug_enabled()) debug_log("prefill_tc D=%d tiles=%lld grid=%lld smem=%d", D, (long long)tiles, (long long)grid, smem);
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB, cu, bmax, emulate_bf16);
+  const int wait_pv = std::getenv("TASFT_PREFILL_WAIT_PV") != nullptr;
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB, cu, bmax, emulate_bf16, wait_pv);
   count_launch();
   return launch_status();
 }
