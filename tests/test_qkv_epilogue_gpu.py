@@ -62,3 +62,14 @@ def test_gate_from_pooled_means_equals_gate_on_tensors():
     hard, kept, _ = T.threshold_scores(b.soft_scores, gate.default_threshold, True)
     assert torch.equal(b.hard_mask, hard) and torch.equal(b.kept.idx, kept.idx)
     assert b.sparsity_ratio == pytest.approx(1.0 - b.hard_mask.float().mean().item())
+
+
+def test_epilogue_larger_block_pooling():
+    g = torch.Generator().manual_seed(9)
+    B, S, Hq, Hk, D = 1, 300, 4, 2, 128
+    ql, kl, vl = (torch.randn(B, S, h * D, generator=g).bfloat16() for h in (Hq, Hk, Hk))
+    cos, sin = _rope_tables(B, S, D, torch.bfloat16, 1)
+    q, k, v, pq, pk = T.qkv_rope_pool(ql.to(DEV), kl.to(DEV), vl.to(DEV), Hq, Hk, cos.to(DEV), sin.to(DEV), 128)
+    rq = O.apply_rotary(ql.view(B, S, Hq, D).transpose(1, 2), cos, sin)
+    assert torch.equal(q.cpu(), rq)
+    assert (pq.cpu() - O.pool_to_blocks(rq.float(), 128)).abs().max().item() <= 1e-6
