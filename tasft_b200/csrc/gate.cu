@@ -188,41 +188,44 @@ __global__ void __launch_bounds__(kPoolThreads, 6) gate_pool_kernel(tasft_gate_a
 }
 
 
-// Pool and project in one pass. Same pooling as gate_pool_kernel (one thread per 16-byte
-// column of a block, CV = D / EPV lanes per block, contiguous in the warp); then each lane
-// forms the partial products of its EPV means with all HID rows of its W_in half (read
-// through L1: the CV lanes of a block read one contiguous row of W per unit), and a
-// butterfly reduce-scatter over the block's CV lanes sums them: lane c ends with the
-// HID / CV units [c * HID / CV, (c + 1) * HID / CV). Saves the means' round trip through
-// HBM and a kernel boundary.
-template <typename T, int EPV, int CV, int HID>
+// Pool and project in one pass. A block's column sums are split over CV * RS lanes of one
+// warp: lane (rs, c) sums the 16-byte column c (EPV elements) over rows rs, rs + RS, ...
+// (so a warp instruction reads RS whole consecutive rows), and shuffles over the RS row
+// groups complete the sums. Then each lane forms the partial products of its EPV means with
+// the HID / RS units of its row group's share of W_in (read through L1), and a butterfly
+// reduce-scatter over the block's CV lanes sums them: lane (rs, c) ends with
+// NOUT = HID / (RS * CV) units. Saves the means' round trip through HBM and a kernel boundary.
+template <typename T, int EPV, int CV, int HID, int RS>
 __global__ void __launch_bounds__(kPoolThreads, 3) gate_pool_project_fused_kernel(tasft_gate_args a, float* A,
                                                                                   float* Ct, int NBq, int NBk) {
   constexpr int D = EPV * CV;
-  constexpr int NOUT = HID / CV;  // units per lane after the reduction
-  static_assert(HID % CV == 0 && (CV & (CV - 1)) == 0 && CV <= 32, "shape");
+  constexpr int HR = HID / RS;     // units per row group
+  constexpr int NOUT = HR / CV;    // units per lane after the reduction
+  static_assert(HR % CV == 0 && (CV & (CV - 1)) == 0 && (RS & (RS - 1)) == 0 && CV * RS <= 32, "shape");
   int t = blockIdx.x * kPoolThreads + threadIdx.x;
-  const int nq = a.B * a.Hq * NBq * CV;
-  const int nk = a.B * a.Hk * NBk * CV;
+  const int nq = a.B * a.Hq * NBq * CV * RS;
+  const int nk = a.B * a.Hk * NBk * CV * RS;
   const bool live = t < nq + nk;
   if (!live) t = nq + nk - 1;  // idle lanes shadow the last block so the shuffles stay full-warp
   const bool isq = t < nq;
   if (!isq) t -= nq;
-  const int c = t & (CV - 1);
-  const int row = t / CV;  // (b * H + h) * NB + blk
+  const int c = t % CV;
+  const int rs = (t / CV) % RS;
+  const int row = t / (CV * RS);  // (b * H + h) * NB + blk
   const int H = isq ? a.Hq : a.Hk, NB = isq ? NBq : NBk, S = isq ? a.Sq : a.Sk;
   const int blk = row % NB, bh = row / NB;
   const int h = bh % H, b = bh / H;
   const int64_t* st = isq ? a.q_stride : a.k_stride;
+  const int64_t rstr = st[2];
   const T* p = reinterpret_cast<const T*>(isq ? a.q : a.k) + b * st[0] + h * st[1] +
-               (int64_t)blk * a.block * st[2] + c * EPV;
+               ((int64_t)blk * a.block + rs) * rstr + c * EPV;
   const int rows = min(a.block, S - blk * a.block);  // padding rows count as zeros
-  const int64_t rs = st[2];
+  const int64_t rs_step = RS * rstr;
   float f[EPV];
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll 8
-    for (int r = 0; r < rows; ++r) add_bf16x8(__ldg(reinterpret_cast<const uint4*>(p + r * rs)), acc);
+    for (int r = rs; r < rows; r += RS, p += rs_step) add_bf16x8(__ldg(reinterpret_cast<const uint4*>(p)), acc);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       f[2 * i] = __uint_as_float((uint32_t)acc[i]);
@@ -232,29 +235,34 @@ __global__ void __launch_bounds__(kPoolThreads, 3) gate_pool_project_fused_kerne
 #pragma unroll
     for (int e = 0; e < EPV; ++e) f[e] = 0.f;
 #pragma unroll 8
-    for (int r = 0; r < rows; ++r) {
+    for (int r = rs; r < rows; r += RS, p += rs_step) {
       float g[EPV];
-      Vec16<T>::unpack(__ldg(reinterpret_cast<const uint4*>(p + r * rs)), g);
+      Vec16<T>::unpack(__ldg(reinterpret_cast<const uint4*>(p)), g);
 #pragma unroll
       for (int e = 0; e < EPV; ++e) f[e] += g[e];
     }
   }
   // this CTA's streaming is done: the pair kernel may launch (it waits for this grid)
   pdl_trigger();
+  // complete the column sums over the RS row groups (lanes CV apart)
+#pragma unroll
+  for (int e = 0; e < EPV; ++e)
+#pragma unroll
+    for (int d = CV; d < CV * RS; d <<= 1) f[e] += __shfl_xor_sync(0xffffffffu, f[e], d);
   const float inv = 1.0f / (float)a.block;
 #pragma unroll
   for (int e = 0; e < EPV; ++e) f[e] *= inv;
   float* pooled = isq ? a.pooled_q : a.pooled_k;
-  if (pooled && live) {
+  if (pooled && live && rs == 0) {
     float* out = pooled + (int64_t)row * D + c * EPV;
 #pragma unroll
     for (int e = 0; e < EPV; e += 4) *reinterpret_cast<float4*>(out + e) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
   }
-  // partial products of this lane's EPV means with every unit
-  float v[HID];
-  const float* w = a.w_in + (isq ? 0 : D) + c * EPV;
+  // partial products of this lane's EPV means with its row group's units [rs * HR, rs * HR + HR)
+  float v[HR];
+  const float* w = a.w_in + (int64_t)rs * HR * 2 * D + (isq ? 0 : D) + c * EPV;
 #pragma unroll
-  for (int j = 0; j < HID; ++j) {
+  for (int j = 0; j < HR; ++j) {
     float s = 0.f;
 #pragma unroll
     for (int e = 0; e < EPV; e += 4) {
@@ -263,14 +271,14 @@ __global__ void __launch_bounds__(kPoolThreads, 3) gate_pool_project_fused_kerne
     }
     v[j] = s;
   }
-  // butterfly reduce-scatter over the CV lanes of this block
-  int n = HID;
+  // butterfly reduce-scatter over the CV lanes of this row group
+  int n = HR;
 #pragma unroll
   for (int d = CV / 2; d >= 1; d >>= 1) {
     const bool upper = (c & d) != 0;
     n >>= 1;
 #pragma unroll
-    for (int i = 0; i < HID / 2; ++i) {
+    for (int i = 0; i < HR / 2; ++i) {
       if (i < n) {
         const float send = upper ? v[i] : v[i + n];
         const float keep = upper ? v[i + n] : v[i];
@@ -279,7 +287,7 @@ __global__ void __launch_bounds__(kPoolThreads, 3) gate_pool_project_fused_kerne
     }
   }
   if (!live) return;
-  const int j0 = c * NOUT;  // lane c holds units [j0, j0 + NOUT)
+  const int j0 = rs * HR + c * NOUT;  // lane (rs, c) holds units [j0, j0 + NOUT)
   if (isq) {
 #pragma unroll
     for (int i = 0; i < NOUT; ++i) A[(int64_t)row * HID + j0 + i] = v[i] + a.b_in[j0 + i];
@@ -606,16 +614,18 @@ static int launch_pool(const tasft_gate_args& a, float* A, float* Ct, float* mq,
   const int64_t nthreads = ((int64_t)a.B * a.Hq * NBq + (int64_t)a.B * a.Hk * NBk) * CV;
   const bool pooled_ok = (!a.pooled_q || aligned16(a.pooled_q)) && (!a.pooled_k || aligned16(a.pooled_k)) &&
                          aligned16(a.w_in);
+  // row groups per block in the fused kernel: a block takes a whole warp (CV * RS = 32)
+  const int RS = 32 / (CV > 0 ? CV : 1);
   if (vec_ok && EPV == 8 && (a.D == 64 || a.D == 128) && (a.hidden == 32 || a.hidden == 64) && pooled_ok &&
-      nthreads < (1LL << 31) - kPoolThreads && !std::getenv("TASFT_GATE_UNFUSED")) {
-    const unsigned blocks = (unsigned)ceil_div(nthreads, kPoolThreads);
+      nthreads * RS < (1LL << 31) - kPoolThreads && !std::getenv("TASFT_GATE_UNFUSED")) {
+    const unsigned blocks = (unsigned)ceil_div(nthreads * RS, kPoolThreads);
     auto go = [&](auto kern) { kern<<<blocks, kPoolThreads, 0, st>>>(a, A, Ct, NBq, NBk); };
     if (a.D == 128) {
-      if (a.hidden == 32) go(gate_pool_project_fused_kernel<T, 8, 16, 32>);
-      else go(gate_pool_project_fused_kernel<T, 8, 16, 64>);
+      if (a.hidden == 32) go(gate_pool_project_fused_kernel<T, 8, 16, 32, 2>);
+      else go(gate_pool_project_fused_kernel<T, 8, 16, 64, 2>);
     } else {
-      if (a.hidden == 32) go(gate_pool_project_fused_kernel<T, 8, 8, 32>);
-      else go(gate_pool_project_fused_kernel<T, 8, 8, 64>);
+      if (a.hidden == 32) go(gate_pool_project_fused_kernel<T, 8, 8, 32, 4>);
+      else go(gate_pool_project_fused_kernel<T, 8, 8, 64, 4>);
     }
   } else if (vec_ok && (CV & (CV - 1)) == 0 && a.D % 4 == 0 && a.D <= 128 && (a.hidden == 32 || a.hidden == 64) &&
       nthreads < (1LL << 31) - kPoolThreads && aligned16(mq) && aligned16(mk)) {

@@ -73,3 +73,28 @@ def test_epilogue_larger_block_pooling():
     rq = O.apply_rotary(ql.view(B, S, Hq, D).transpose(1, 2), cos, sin)
     assert torch.equal(q.cpu(), rq)
     assert (pq.cpu() - O.pool_to_blocks(rq.float(), 128)).abs().max().item() <= 1e-6
+
+
+@pytest.mark.parametrize("case", ["fused_proj_shared_tables", "no_rope", "short_sequence"])
+def test_epilogue_layouts(case):
+    """q/k/v as column slices of one fused [B, S, (Hq + 2 Hk) * D] projection (token stride
+    larger than the row), rotary tables shared over the batch, no rotary, S below a block."""
+    B, S, Hq, Hk, D = (3, 200, 8, 2, 128) if case != "short_sequence" else (2, 40, 4, 1, 64)
+    g = torch.Generator().manual_seed(11)
+    fused = torch.randn(B, S, (Hq + 2 * Hk) * D, generator=g).bfloat16()
+    ql, kl, vl = fused.split([Hq * D, Hk * D, Hk * D], dim=-1)
+    cos, sin = _rope_tables(1, S, D, torch.bfloat16, 5)
+    fd = fused.to(DEV)
+    qd, kd, vd = fd.split([Hq * D, Hk * D, Hk * D], dim=-1)
+    rope = case != "no_rope"
+    q, k, v, pq, pk = T.qkv_rope_pool(qd, kd, vd, Hq, Hk, cos.to(DEV) if rope else None,
+                                      sin.to(DEV) if rope else None, 64)
+    xq = ql.reshape(B, S, Hq, D).transpose(1, 2)
+    xk = kl.reshape(B, S, Hk, D).transpose(1, 2)
+    rq = O.apply_rotary(xq, cos, sin) if rope else xq
+    rk = O.apply_rotary(xk, cos, sin) if rope else xk
+    assert torch.equal(q.cpu(), rq)
+    assert torch.equal(k.cpu(), rk)
+    assert torch.equal(v.cpu(), vl.reshape(B, S, Hk, D).transpose(1, 2))
+    assert (pq.cpu() - O.pool_to_blocks(rq.float(), 64)).abs().max().item() <= 1e-6
+    assert (pk.cpu() - O.pool_to_blocks(rk.float(), 64)).abs().max().item() <= 1e-6
