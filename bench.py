@@ -812,6 +812,15 @@ def run_ours(args):
         t_n = time_steps(lambda: dec_n(ql, kl_loc, vl_loc, kvl, lkept, lo, local=lloc), args.steps, args.warmup,
                          flush, ws)
         long_extra["ms_per_token_nccl_eager"] = round(max_over_ranks(statistics.mean(t_n), ws), 4)
+        # where the step's time goes: this rank's local split decode alone (graph replay)
+        t_loc = time_steps(graphed(lambda: T.bsa_decode(ql, kl_loc, vl_loc, SH.local_kv_len(kvl, lo, hi, lc["block"]),
+                                                         lloc, lc["block"], workspace=dec.ws,
+                                                         partials=(dec.po, dec.pm))),
+                           args.steps, args.warmup, flush, ws)
+        long_extra["ms_local_decode_only"] = round(max_over_ranks(statistics.mean(t_loc), ws), 4)
+        # and the peer-memory merge alone (every rank replays it, so the ranks still meet)
+        t_mrg = time_steps(graphed(lambda: dec.peer(dec.po, dec.pm, dec.out)), args.steps, args.warmup, flush, ws)
+        long_extra["ms_merge_only"] = round(max_over_ranks(statistics.mean(t_mrg), ws), 4)
     else:
         # one GPU: the step replayed from a CUDA graph, as a serving loop would run it (its
         # Python launch path takes longer than the ~20 us of kernels)
