@@ -824,7 +824,8 @@ def run_ours(args):
     else:
         # one GPU: the step replayed from a CUDA graph, as a serving loop would run it (its
         # Python launch path takes longer than the ~20 us of kernels)
-        lstep = graphed(lambda: T.bsa_decode(ql, kl_loc, vl_loc, kvl, lkept, lc["block"]))
+        lws = T.DecodeWorkspace(lc["B"], lc["Hq"], lc["Hk"], lc["D"], 64, dev)  # kept across steps
+        lstep = graphed(lambda: T.bsa_decode(ql, kl_loc, vl_loc, kvl, lkept, lc["block"], workspace=lws))
         ltiming = "CUDA graph replay"
     t_long = time_steps(lstep, args.steps, args.warmup, flush, ws)
     ms_l = max_over_ranks(statistics.mean(t_long), ws)

@@ -416,7 +416,11 @@ int decode_pick_splits(const tasft_decode_args& a) {
     const int units = a.B * a.Hk;
     nsplit = (6 * 148) / units;  // items within the resident CTA slots
     int cap = a.nb_max / 4 > 1 ? a.nb_max / 4 : 1;
-    if (cap > 16) cap = 16;  // the last split merges all partials with one warp
+    // the scalar path merges in the last split (one warp, up to 16); the tensor-core path
+    // merges wide splits in a separate kernel, so few units (one long sequence) can still
+    // spread over the SMs
+    const int most = decode_mma_ok(a) ? 64 : 16;
+    if (cap > most) cap = most;
     if (nsplit > cap) nsplit = cap;
     if (nsplit < 1) nsplit = 1;
   }

@@ -82,6 +82,8 @@ __device__ void decode_finish(const tasft_decode_args& a, const DecodeWs& ws, in
   }
 }
 
+// whether the tensor-core decode takes these arguments (bf16/f16, block 64, D 64/128, group <= 8)
+bool decode_mma_ok(const tasft_decode_args& a);
 int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st);
 // Paged-cache variant (k_cache / v_cache are page pools, see tasft_bsa_decode_paged_fwd).
 int decode_mma_paged(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const int32_t* table, int max_pages,

@@ -31,6 +31,9 @@ constexpr int kStages = 2;
 constexpr int kBlkM = 64;        // kv block (list granularity)
 constexpr int kSub = 32;         // keys per ring stage (half a block)
 constexpr int kCtasPerSm = 6;
+// up to this many splits the last split of a unit merges them (one warp); above it a
+// separate merge kernel does (decode_merge_kernel)
+constexpr int kInlineMergeMaxSplits = 16;
 constexpr float kLog2eM = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -120,7 +123,8 @@ __device__ __forceinline__ uint32_t movm_t(uint32_t x) {
 template <int D, bool kF16, bool kPaged>
 __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
     bsa_decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                          const tasft_decode_args a, const DecodeWs ws, const int nsplit, const PagedInfo pg) {
+                          const tasft_decode_args a, const DecodeWs ws, const int nsplit, const PagedInfo pg,
+                          const int merge_inline) {
   using T = typename std::conditional<kF16, __half, __nv_bfloat16>::type;
   constexpr int kTile = (D / 64) * kSub * 128;  // bytes of one K (or V) half-block tile
   constexpr int kStage = 2 * kTile;
@@ -148,6 +152,9 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
     fence_barrier_init();
   }
   __syncthreads();
+  // a merge kernel launched behind this one (wide splits) may start its CTAs now; they
+  // wait for this grid to complete before reading the partials
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 1) {
     // ---------------- producer: streams every claimed item's half-blocks ----------------
@@ -403,6 +410,7 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
           pr[D + 1] = L[e];
         }
       }
+      if (!merge_inline) continue;  // wide splits: decode_merge_kernel merges after this grid
       __threadfence();
       __syncwarp();
       int last = 0;
@@ -475,6 +483,83 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
   __syncwarp();
 }
 
+// Merge of wide splits: one CTA per q-head row, launched behind the decode grid with
+// programmatic dependent launch (its CTAs are resident early and wait on the grid). The
+// four warps take every fourth split; lane l holds d = 64 i + 2 l + {0, 1} (8-byte loads:
+// a partial row is D + 2 floats, so rows are only 8-byte aligned), all of a warp's
+// partial rows are independent loads. The max over the splits comes first (threads over
+// splits), the weighted sums meet in shared memory. Same maths as the in-kernel merge:
+// o = sum_s l_s e^(m_s - m) o_s / sum_s l_s e^(m_s - m).
+constexpr int kMergeThreads = 128;
+
+template <int D, bool kF16>
+__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const tasft_decode_args a, const DecodeWs ws,
+                                                                      const int nsplit) {
+  using T = typename std::conditional<kF16, __half, __nv_bfloat16>::type;
+  constexpr int kW = kMergeThreads / 32;
+  constexpr int DP = D / 64;  // float2 per lane
+  __shared__ float s_max[kW];
+  __shared__ float s_num[kW][D];
+  __shared__ float s_den[kW];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int64_t row = blockIdx.x;  // b * Hq + hq
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* pr = ws.part + row * ws.max_splits * (D + 2);
+  float mt = -INFINITY;
+  for (int sp = threadIdx.x; sp < nsplit; sp += kMergeThreads)
+    if (__ldcg(pr + sp * (D + 2) + D + 1) > 0.f) mt = fmaxf(mt, __ldcg(pr + sp * (D + 2) + D));
+  mt = warp_max(mt);
+  if (lane == 0) s_max[warp] = mt;
+  __syncthreads();
+  mt = s_max[0];
+#pragma unroll
+  for (int w = 1; w < kW; ++w) mt = fmaxf(mt, s_max[w]);
+  float2 num[DP];
+#pragma unroll
+  for (int i = 0; i < DP; ++i) num[i] = make_float2(0.f, 0.f);
+  float den = 0.f;
+#pragma unroll 4
+  for (int sp = warp; sp < nsplit; sp += kW) {
+    const float* ps = pr + sp * (D + 2);
+    const float lv = __ldcg(ps + D + 1);
+    const float mv = __ldcg(ps + D);
+    float2 v[DP];
+#pragma unroll
+    for (int i = 0; i < DP; ++i) v[i] = __ldcg(reinterpret_cast<const float2*>(ps + i * 64) + lane);
+    const float w = lv > 0.f ? lv * __expf(mv - mt) : 0.f;
+    den += w;
+#pragma unroll
+    for (int i = 0; i < DP; ++i) {
+      num[i].x = fmaf(w, v[i].x, num[i].x);
+      num[i].y = fmaf(w, v[i].y, num[i].y);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < DP; ++i) {
+    s_num[warp][i * 64 + 2 * lane] = num[i].x;
+    s_num[warp][i * 64 + 2 * lane + 1] = num[i].y;
+  }
+  if (lane == 0) s_den[warp] = den;
+  __syncthreads();
+  float dt = 0.f;
+#pragma unroll
+  for (int w = 0; w < kW; ++w) dt += s_den[w];
+  const float inv = dt > 0.f ? 1.f / dt : 0.f;
+  const int b = (int)(row / a.Hq), hq = (int)(row % a.Hq);
+  for (int d = threadIdx.x; d < D; d += kMergeThreads) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kW; ++w) t += s_num[w][d];
+    const float ov = t * inv;
+    if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(ov);
+    if (a.part_o) a.part_o[row * D + d] = ov;
+  }
+  if (a.part_ml && threadIdx.x == 0) {
+    a.part_ml[row * 2] = mt;
+    a.part_ml[row * 2 + 1] = dt;
+  }
+}
+
 template <int D, bool kF16, bool kPaged>
 int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const PagedInfo& pg, cudaStream_t st) {
   CUtensorMap mk, mv;
@@ -508,7 +593,22 @@ int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const
   if (debug_enabled())
     debug_log("decode_mma D=%d f16=%d paged=%d grid=%lld smem=%d splits=%d", D, (int)kF16, (int)kPaged,
               (long long)grid, smem, nsplit);
-  kern<<<(unsigned)grid, kThreadsM, smem, st>>>(mk, mv, a, ws, nsplit, pg);
+  const int inline_merge = nsplit <= kInlineMergeMaxSplits;
+  kern<<<(unsigned)grid, kThreadsM, smem, st>>>(mk, mv, a, ws, nsplit, pg, inline_merge);
+  count_launch();
+  if (inline_merge) return launch_status();
+  // wide splits: the merge kernel, its launch overlapped with the decode grid
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(a.B * a.Hq));
+  cfg.blockDim = dim3(kMergeThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, decode_merge_kernel<D, kF16>, a, ws, nsplit) != cudaSuccess) return launch_status();
   count_launch();
   return launch_status();
 }
@@ -532,6 +632,8 @@ int dispatch(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const P
 }
 
 }  // namespace
+
+bool decode_mma_ok(const tasft_decode_args& a) { return mma_ok(a); }
 
 int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st) {
   return dispatch<false>(a, ws, nsplit, PagedInfo{nullptr, 0, 0, 0}, st);

@@ -25,18 +25,25 @@ class DecodeWorkspace:
         self.key = (B, Hq, Hk, D)
 
 
-def default_splits(B: int, Hk: int, mean_kept: float, sms: int = 148) -> int:
+def max_splits_for(dtype: torch.dtype, block: int, D: int, group: int) -> int:
+    """Most splits the decode takes: 64 on the tensor-core path (bf16/f16, block 64, D 64 or
+    128, group <= 8), whose wide splits merge in a separate kernel; 16 elsewhere (the last
+    split of a unit merges all partials with one warp)."""
+    mma = dtype in (torch.bfloat16, torch.float16) and block == 64 and D in (64, 128) and group <= 8
+    return 64 if mma else 16
+
+
+def default_splits(B: int, Hk: int, mean_kept: float, sms: int = 148, most: int = 16) -> int:
     """Splits per (sequence, kv-head) for the persistent decode kernel.
 
     As many splits as keep the work items within the resident CTA slots (6 per SM), so
     each CTA owns one item and no dynamic claiming is needed; at least two kept blocks
-    per split, at most 16 splits (the last split of a unit merges all partials with one
-    warp, and past 16 that merge costs more than the extra parallelism gains).
+    per split, at most ``most`` (``max_splits_for``).
     """
     units = max(1, B * Hk)
     fit = max(1, (6 * sms) // units)
     by_size = max(1, int(mean_kept // 2))
-    return max(1, min(fit, by_size, 16))
+    return max(1, min(fit, by_size, most))
 
 
 def _decode_args(q, k, v, kv_len, kept: KeptBlocks, block, L_logical, Hk, num_splits, workspace, out, partials,
@@ -48,12 +55,13 @@ def _decode_args(q, k, v, kv_len, kept: KeptBlocks, block, L_logical, Hk, num_sp
     cnt = kept.cnt.contiguous()
     ws_ptr, ws_bytes = None, 0
     if num_splits != 1:
+        most = max_splits_for(q.dtype, block, D, Hq // Hk)
         if workspace is None:
-            ms = num_splits if num_splits > 0 else 16
+            ms = num_splits if num_splits > 0 else most
             workspace = DecodeWorkspace(B, Hq, Hk, D, ms, q.device)
         ws_ptr, ws_bytes = workspace.buf.data_ptr(), workspace.bytes
         if num_splits <= 0:
-            num_splits = min(workspace.max_splits, default_splits(B, Hk, idx.shape[-1] / 4))
+            num_splits = min(workspace.max_splits, default_splits(B, Hk, idx.shape[-1] / 4, most=most))
     args = L.DecodeArgs(
         q=q.data_ptr(), k_cache=k.data_ptr(), v_cache=v.data_ptr(), out=L.ptr(out),
         q_stride=L.strides3(q), k_stride=L.strides4(k), v_stride=L.strides4(v),

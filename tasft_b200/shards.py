@@ -264,7 +264,7 @@ class SplitKVDecoder:
         # "peer": partials merged over peer memory by one kernel (graph-capturable step)
         self.peer = PeerExchange(B * Hq, D, device, group) if exchange == "peer" else None
         self.out = torch.empty(B, Hq, D, dtype=out_dtype, device=device) if self.peer is not None else None
-        self.ws = DecodeWorkspace(B, Hq, Hk, D, max(num_splits, 16), device)
+        self.ws = DecodeWorkspace(B, Hq, Hk, D, max(num_splits, 64), device)
         self.no, self.nm = B * Hq * D, B * Hq * 2
         self.flat = torch.empty(self.no + self.nm, dtype=torch.float32, device=device)
         self.po = self.flat[: self.no].view(B, Hq, D)

@@ -273,6 +273,30 @@ class TestDecode:
                             T.KeptBlocks(idx.to(DEV), cnt.to(DEV)), num_splits=splits, workspace=ws)
         assert torch.equal(out, out2)
 
+    @pytest.mark.parametrize("splits,D,grp", [(24, 128, 7), (64, 128, 7), (40, 64, 8), (0, 128, 7)])
+    def test_wide_splits_separate_merge(self, splits, D, grp):
+        """More than 16 splits: the decode grid writes every split's partial and a merge
+        kernel (launched behind it) combines them; one long sequence (the configs[3]
+        shape at a smaller L), ragged lengths, splits with nothing kept, then the same
+        call twice (partials are rewritten, no state carried over)."""
+        B, Hk = 2, 4
+        q, kc, vc, kv_len, idx, cnt = _decode_case(B, grp * Hk, Hk, 4096, D, torch.bfloat16, 0.1, 31,
+                                                   lens=[4096, 2500])
+        kept = T.KeptBlocks(idx.to(DEV), cnt.to(DEV))
+        ws = T.DecodeWorkspace(B, grp * Hk, Hk, D, 64, DEV)
+        run = lambda: T.bsa_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), kv_len.to(DEV), kept, num_splits=splits,
+                                   workspace=ws)
+        out = run()
+        ref = O.bsa_decode(q, kc, vc, kv_len, idx, cnt, 64)
+        assert_bf16_close(out, ref)
+        assert torch.equal(out, run())
+        # the merged (o, m, l) for a cross-GPU combine agree with the output
+        po = torch.empty(B, grp * Hk, D, device=DEV)
+        pm = torch.empty(B, grp * Hk, 2, device=DEV)
+        T.bsa_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), kv_len.to(DEV), kept, num_splits=splits, workspace=ws,
+                     partials=(po, pm))
+        assert (po.bfloat16().float() - out.float()).abs().max().item() <= 1e-2
+
     def test_dynamic_claiming_more_items_than_ctas(self):
         """1536 work items > resident CTAs: items are claimed from the workspace counter,
         which must be back at zero for the next call."""
