@@ -484,11 +484,12 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
 }
 
 // Merge of wide splits: one CTA per q-head row, launched behind the decode grid with
-// programmatic dependent launch (its CTAs are resident early and wait on the grid). The
-// four warps take every fourth split; lane l holds d = 64 i + 2 l + {0, 1} (8-byte loads:
-// a partial row is D + 2 floats, so rows are only 8-byte aligned), all of a warp's
-// partial rows are independent loads. The max over the splits comes first (threads over
-// splits), the weighted sums meet in shared memory. Same maths as the in-kernel merge:
+// programmatic dependent launch (its CTAs are resident early and wait on the grid). Warp w
+// takes splits w, w + 4, ...; lane l holds d = 64 i + 2 l + {0, 1} (8-byte loads: a
+// partial row is D + 2 floats, so rows are only 8-byte aligned). A warp loads up to 16 of
+// its partial rows at once, merges them against its own running max, and the four warps'
+// results are rescaled to the common max in shared memory, so the row costs one round
+// trip to L2 per 64 splits. Same maths as the in-kernel merge:
 // o = sum_s l_s e^(m_s - m) o_s / sum_s l_s e^(m_s - m).
 constexpr int kMergeThreads = 128;
 
@@ -498,6 +499,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const tasft
   using T = typename std::conditional<kF16, __half, __nv_bfloat16>::type;
   constexpr int kW = kMergeThreads / 32;
   constexpr int DP = D / 64;  // float2 per lane
+  constexpr int kBatch = 16;  // partial rows a warp has in flight
   __shared__ float s_max[kW];
   __shared__ float s_num[kW][D];
   __shared__ float s_den[kW];
@@ -505,33 +507,49 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const tasft
   const int64_t row = blockIdx.x;  // b * Hq + hq
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* pr = ws.part + row * ws.max_splits * (D + 2);
-  float mt = -INFINITY;
-  for (int sp = threadIdx.x; sp < nsplit; sp += kMergeThreads)
-    if (__ldcg(pr + sp * (D + 2) + D + 1) > 0.f) mt = fmaxf(mt, __ldcg(pr + sp * (D + 2) + D));
-  mt = warp_max(mt);
-  if (lane == 0) s_max[warp] = mt;
-  __syncthreads();
-  mt = s_max[0];
-#pragma unroll
-  for (int w = 1; w < kW; ++w) mt = fmaxf(mt, s_max[w]);
+  float mw = -INFINITY, den = 0.f;
   float2 num[DP];
 #pragma unroll
   for (int i = 0; i < DP; ++i) num[i] = make_float2(0.f, 0.f);
-  float den = 0.f;
-#pragma unroll 4
-  for (int sp = warp; sp < nsplit; sp += kW) {
-    const float* ps = pr + sp * (D + 2);
-    const float lv = __ldcg(ps + D + 1);
-    const float mv = __ldcg(ps + D);
-    float2 v[DP];
+  for (int s0 = warp; s0 < nsplit; s0 += kBatch * kW) {
+    float lv[kBatch], mv[kBatch];
+    float2 v[kBatch][DP];
 #pragma unroll
-    for (int i = 0; i < DP; ++i) v[i] = __ldcg(reinterpret_cast<const float2*>(ps + i * 64) + lane);
-    const float w = lv > 0.f ? lv * __expf(mv - mt) : 0.f;
-    den += w;
+    for (int k = 0; k < kBatch; ++k) {
+      const int sp = s0 + k * kW;
+      lv[k] = 0.f;
+      mv[k] = -INFINITY;
+      if (sp < nsplit) {
+        const float* ps = pr + sp * (D + 2);
+        lv[k] = __ldcg(ps + D + 1);
+        mv[k] = __ldcg(ps + D);
+#pragma unroll
+        for (int i = 0; i < DP; ++i) v[k][i] = __ldcg(reinterpret_cast<const float2*>(ps + i * 64) + lane);
+      }
+    }
+    float mb = mw;
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k)
+      if (lv[k] > 0.f) mb = fmaxf(mb, mv[k]);
+    if (mb == -INFINITY) continue;  // nothing kept in these splits yet
+    const float sc = mw == -INFINITY ? 0.f : __expf(mw - mb);  // rescale what came before
+    den *= sc;
 #pragma unroll
     for (int i = 0; i < DP; ++i) {
-      num[i].x = fmaf(w, v[i].x, num[i].x);
-      num[i].y = fmaf(w, v[i].y, num[i].y);
+      num[i].x *= sc;
+      num[i].y *= sc;
+    }
+    mw = mb;
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      if (!(lv[k] > 0.f)) continue;
+      const float w = lv[k] * __expf(mv[k] - mw);
+      den += w;
+#pragma unroll
+      for (int i = 0; i < DP; ++i) {
+        num[i].x = fmaf(w, v[k][i].x, num[i].x);
+        num[i].y = fmaf(w, v[k][i].y, num[i].y);
+      }
     }
   }
 #pragma unroll
@@ -539,17 +557,27 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const tasft
     s_num[warp][i * 64 + 2 * lane] = num[i].x;
     s_num[warp][i * 64 + 2 * lane + 1] = num[i].y;
   }
-  if (lane == 0) s_den[warp] = den;
+  if (lane == 0) {
+    s_max[warp] = mw;
+    s_den[warp] = den;
+  }
   __syncthreads();
+  float mt = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kW; ++w) mt = fmaxf(mt, s_max[w]);
+  float scw[kW];
   float dt = 0.f;
 #pragma unroll
-  for (int w = 0; w < kW; ++w) dt += s_den[w];
+  for (int w = 0; w < kW; ++w) {
+    scw[w] = s_max[w] == -INFINITY ? 0.f : __expf(s_max[w] - mt);
+    dt += scw[w] * s_den[w];
+  }
   const float inv = dt > 0.f ? 1.f / dt : 0.f;
   const int b = (int)(row / a.Hq), hq = (int)(row % a.Hq);
   for (int d = threadIdx.x; d < D; d += kMergeThreads) {
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < kW; ++w) t += s_num[w][d];
+    for (int w = 0; w < kW; ++w) t += scw[w] * s_num[w][d];
     const float ov = t * inv;
     if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(ov);
     if (a.part_o) a.part_o[row * D + d] = ov;
