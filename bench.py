@@ -813,9 +813,8 @@ def run_ours(args):
                          flush, ws)
         long_extra["ms_per_token_nccl_eager"] = round(max_over_ranks(statistics.mean(t_n), ws), 4)
         # where the step's time goes: this rank's local split decode alone (graph replay)
-        t_loc = time_steps(graphed(lambda: T.bsa_decode(ql, kl_loc, vl_loc, SH.local_kv_len(kvl, lo, hi, lc["block"]),
-                                                         lloc, lc["block"], workspace=dec.ws,
-                                                         partials=(dec.po, dec.pm))),
+        t_loc = time_steps(graphed(lambda: T.bsa_decode(ql, kl_loc, vl_loc, kvl, lloc, lc["block"], workspace=dec.ws,
+                                                         partials=(dec.po, dec.pm), kv_offset=lo * lc["block"])),
                            args.steps, args.warmup, flush, ws)
         long_extra["ms_local_decode_only"] = round(max_over_ranks(statistics.mean(t_loc), ws), 4)
         # and the peer-memory merge alone (every rank replays it, so the ranks still meet)

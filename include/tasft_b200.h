@@ -246,6 +246,8 @@ typedef struct {
   void* workspace;        /* tasft_decode_workspace_size() bytes; the call clears its ticket prefix */
   int64_t workspace_bytes;
   int32_t* err;
+  int32_t kv_offset;      /* tokens before this cache's first row (one rank's slab of a longer
+                             sequence): valid rows = clamp(kv_len - kv_offset, 0, L); 0 otherwise */
 } tasft_decode_args;
 TASFT_API int64_t tasft_decode_workspace_size(int32_t B, int32_t Hq, int32_t Hk, int32_t D, int32_t max_splits);
 TASFT_API int tasft_bsa_decode_fwd(const tasft_decode_args* args, tasft_stream_t stream);
@@ -309,8 +311,8 @@ typedef struct {
   const float* part_o;    /* [rows, D] this rank's normalised partial output */
   const float* part_ml;   /* [rows, 2] its (m, l), base e */
   int64_t rows;           /* B * Hq */
-  int32_t D;
-  int32_t world, rank;
+  int32_t D;              /* even; part_o and part_ml 8-byte aligned */
+  int32_t world, rank;    /* world <= 8 (one NVLink node) */
   void* const* mailboxes; /* device array [world] of device pointers: rank r's mailbox (own or IPC-mapped) */
   uint32_t* epoch;        /* device scalar of this rank, zero before the first call */
   void* out;              /* [rows, D] dtype */

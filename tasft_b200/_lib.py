@@ -101,6 +101,7 @@ class DecodeArgs(C.Structure):
         ("block", C.c_int32), ("dtype", C.c_int32), ("scale", C.c_float),
         ("kv_len", vp), ("kept_idx", vp), ("kept_cnt", vp), ("nb_max", C.c_int32), ("num_splits", C.c_int32),
         ("part_o", vp), ("part_ml", vp), ("workspace", vp), ("workspace_bytes", C.c_int64), ("err", vp),
+        ("kv_offset", C.c_int32),
     ]
 
 

@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(kDecThreads) bsa_decode_simt_kernel(tasft_deco
   const int t0 = (int)((int64_t)split * cnt_all / nsplit);
   const int t1 = (int)((int64_t)(split + 1) * cnt_all / nsplit);
   const int32_t* list = a.kept_idx + ((int64_t)b * a.Hk + hk) * a.nb_max;
-  const int kvlen = min(a.kv_len[b], a.L);
+  const int kvlen = max(0, min(a.kv_len[b] - a.kv_offset, a.L));
   const int NBk = (a.L + BLK - 1) / BLK;
 
   if (threadIdx.x == 0) {

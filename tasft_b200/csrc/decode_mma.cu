@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
       const int b = unit / a.Hk, hk = unit % a.Hk;
       if (t.item != cur) {
         cur = t.item;
-        kvlen = min(a.kv_len[b], a.L);
+        kvlen = max(0, min(a.kv_len[b] - a.kv_offset, a.L));
         const T* qh = reinterpret_cast<const T*>(a.q) + b * a.q_stride[0] + (int64_t)(hk * grp + g) * a.q_stride[1];
         const bool hv = g < grp;
 #pragma unroll

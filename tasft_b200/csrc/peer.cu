@@ -34,6 +34,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 __host__ __device__ inline int64_t flags_bytes(int world) { return ((int64_t)world * 4 + 255) / 256 * 256; }
 
+constexpr int kRowChunk = 128;  // rows whose merge weights sit in shared memory at once
+constexpr int kMaxWorld = 8;
+
 template <typename T>
 __global__ void __launch_bounds__(kPeerThreads) peer_combine_kernel(tasft_peer_combine_args a) {
   const int world = a.world, rank = a.rank, D = a.D;
@@ -42,12 +45,16 @@ __global__ void __launch_bounds__(kPeerThreads) peer_combine_kernel(tasft_peer_c
   const uint32_t e = *a.epoch + 1u;
   const int par = (int)(e & 1u);
   const int64_t foff = flags_bytes(world) / 4;  // float offset of the partials
-  // 1. push this rank's (o | m, l) rows into slot [par][rank] of every mailbox
+  // 1. push this rank's (o | m, l) rows into slot [par][rank] of every mailbox, 8 bytes per
+  //    store (a row is D + 2 floats, D even: rows stay 8-byte aligned)
+  const int64_t rp = (D + 2) / 2;  // float2 per mailbox row
   for (int p = 0; p < world; ++p) {
-    float* dst = reinterpret_cast<float*>(a.mailboxes[p]) + foff + ((int64_t)par * world + rank) * slab;
-    for (int64_t x = threadIdx.x; x < slab; x += blockDim.x) {
-      const int64_t r = x / (D + 2), c = x % (D + 2);
-      dst[x] = c < D ? a.part_o[r * D + c] : a.part_ml[r * 2 + (c - D)];
+    float2* dst = reinterpret_cast<float2*>(reinterpret_cast<float*>(a.mailboxes[p]) + foff +
+                                            ((int64_t)par * world + rank) * slab);
+    for (int64_t x = threadIdx.x; x < rows * rp; x += blockDim.x) {
+      const int64_t r = x / rp, c = x % rp;
+      dst[x] = c < D / 2 ? reinterpret_cast<const float2*>(a.part_o + r * D)[c]
+                         : reinterpret_cast<const float2*>(a.part_ml)[r];
     }
   }
   __syncthreads();
@@ -72,29 +79,45 @@ __global__ void __launch_bounds__(kPeerThreads) peer_combine_kernel(tasft_peer_c
   }
   __syncthreads();
   if (s_timeout && threadIdx.x == 0) set_err(a.err, TASFT_DEVERR_TIMEOUT);
-  // 4. merge the world partials of this parity
+  // 4. merge the world partials of this parity: per chunk of rows, the weights
+  //    w_g = l_g e^(m_g - max) and their sum first (all (rank, row) pairs loaded at once), then every
+  //    output element as one pass of independent loads
   const float* box = reinterpret_cast<const float*>(a.mailboxes[rank]) + foff + (int64_t)par * world * slab;
-  for (int64_t x = threadIdx.x; x < rows * D; x += blockDim.x) {
-    const int64_t r = x / D;
-    const int c = (int)(x % D);
-    float mt = -INFINITY;
-    for (int g = 0; g < world; ++g) {
-      const float* pr = box + g * slab + r * (D + 2);
-      if (pr[D + 1] > 0.f) mt = fmaxf(mt, pr[D]);
-    }
-    float num = 0.f, den = 0.f;
-    for (int g = 0; g < world; ++g) {
-      const float* pr = box + g * slab + r * (D + 2);
+  __shared__ float s_w[kMaxWorld][kRowChunk];
+  __shared__ float s_m[kMaxWorld][kRowChunk];
+  __shared__ float s_den[kRowChunk];
+  for (int64_t r0 = 0; r0 < rows; r0 += kRowChunk) {
+    const int nr = rows - r0 < kRowChunk ? (int)(rows - r0) : kRowChunk;
+    for (int x = threadIdx.x; x < world * nr; x += blockDim.x) {
+      const int g = x / nr, r = x % nr;
+      const float* pr = box + g * slab + (r0 + r) * (D + 2);
       const float l = pr[D + 1];
-      if (l > 0.f) {
-        const float w = l * __expf(pr[D] - mt);
-        num = fmaf(w, pr[c], num);
+      s_w[g][r] = l;
+      s_m[g][r] = l > 0.f ? pr[D] : -INFINITY;
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < nr; r += blockDim.x) {
+      float mt = -INFINITY;
+      for (int g = 0; g < world; ++g) mt = fmaxf(mt, s_m[g][r]);
+      float den = 0.f;
+      for (int g = 0; g < world; ++g) {
+        const float w = s_m[g][r] == -INFINITY ? 0.f : s_w[g][r] * __expf(s_m[g][r] - mt);
+        s_w[g][r] = w;
         den += w;
       }
+      s_den[r] = den;
     }
-    reinterpret_cast<T*>(a.out)[x] = from_f<T>(den > 0.f ? num / den : 0.f);
+    __syncthreads();
+#pragma unroll 4
+    for (int x = threadIdx.x; x < nr * D; x += blockDim.x) {
+      const int r = x / D, c = x % D;
+      float num = 0.f;
+      for (int g = 0; g < world; ++g) num = fmaf(s_w[g][r], box[g * slab + (r0 + r) * (D + 2) + c], num);
+      const float den = s_den[r];
+      reinterpret_cast<T*>(a.out)[(r0 + r) * D + c] = from_f<T>(den > 0.f ? num / den : 0.f);
+    }
+    __syncthreads();
   }
-  __syncthreads();
   if (threadIdx.x == 0) *a.epoch = e;
 }
 
@@ -145,7 +168,10 @@ extern "C" int tasft_peer_combine(const tasft_peer_combine_args* ap, tasft_strea
   if (!ap) return TASFT_ERR_INVALID_ARG;
   const tasft_peer_combine_args& a = *ap;
   if (!a.part_o || !a.part_ml || !a.mailboxes || !a.epoch || !a.out) return TASFT_ERR_INVALID_ARG;
-  if (a.world <= 0 || a.world > kPeerThreads || a.rank < 0 || a.rank >= a.world || a.rows <= 0 || a.D <= 0)
+  if (a.world <= 0 || a.world > kMaxWorld || a.rank < 0 || a.rank >= a.world || a.rows <= 0 || a.D <= 0)
+    return TASFT_ERR_INVALID_ARG;
+  // 8-byte pushes: D even, partial rows 8-byte aligned
+  if ((a.D & 1) || (reinterpret_cast<uintptr_t>(a.part_o) & 7u) || (reinterpret_cast<uintptr_t>(a.part_ml) & 7u))
     return TASFT_ERR_INVALID_ARG;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (a.dtype) {

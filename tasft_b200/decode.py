@@ -47,7 +47,7 @@ def default_splits(B: int, Hk: int, mean_kept: float, sms: int = 148, most: int 
 
 
 def _decode_args(q, k, v, kv_len, kept: KeptBlocks, block, L_logical, Hk, num_splits, workspace, out, partials,
-                 err):
+                 err, kv_offset: int = 0):
     """The ``tasft_decode_args`` both decode entry points share (``k``/``v`` are the caches,
     or the page pools for the paged call), with the split count and workspace resolved."""
     B, Hq, D = q.shape
@@ -70,7 +70,7 @@ def _decode_args(q, k, v, kv_len, kept: KeptBlocks, block, L_logical, Hk, num_sp
         kv_len=kv_len.data_ptr(), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(), nb_max=idx.shape[-1],
         num_splits=num_splits, part_o=L.ptr(partials[0]) if partials else None,
         part_ml=L.ptr(partials[1]) if partials else None, workspace=ws_ptr, workspace_bytes=ws_bytes,
-        err=L.ptr(err),
+        err=L.ptr(err), kv_offset=int(kv_offset),
     )
     # keep the tensors the struct points into alive until the call returns
     return args, num_splits, (idx, cnt, workspace)
@@ -89,11 +89,14 @@ def bsa_decode(
     out: torch.Tensor | None = None,
     partials: tuple[torch.Tensor, torch.Tensor] | None = None,
     err: torch.Tensor | None = None,
+    kv_offset: int = 0,
 ) -> torch.Tensor | None:
     """Decode attention: q ``[B,Hq,D]``, caches ``[B,Hk,L,D]``, ``kv_len`` int32 ``[B]``,
     ``kept`` lists ``[B,Hk,NBmax]`` / ``[B,Hk]``. Returns ``[B,Hq,D]`` (``out``) and, when
     ``partials=(o [B,Hq,D] f32, ml [B,Hq,2] f32)`` is given, also writes the normalised
-    output with its (max, sum) for a cross-GPU combine."""
+    output with its (max, sum) for a cross-GPU combine. ``kv_offset``: the cache is the slab
+    of a longer sequence starting at that token (one rank's share of a split cache); the
+    valid rows are ``clamp(kv_len - kv_offset, 0, L)``, computed in the kernel."""
     L.require_cuda(q, k_cache, v_cache, kv_len)
     if q.ndim != 3 or k_cache.ndim != 4 or k_cache.shape != v_cache.shape:
         raise KernelError("decode expects q [B,Hq,D] and caches [B,Hk,L,D]",
@@ -108,7 +111,7 @@ def bsa_decode(
     if out is None and partials is None:
         out = torch.empty_like(q)
     args, num_splits, _keep = _decode_args(q, k_cache, v_cache, kv_len, kept, block, Lc, Hk, num_splits, workspace,
-                                           out, partials, err)
+                                           out, partials, err, kv_offset)
     L.check(L.lib().tasft_bsa_decode_fwd(args, L.stream_ptr(q.device)), "tasft_bsa_decode_fwd",
             shape=[B, Hq, Hk, Lc, D], splits=num_splits)
     return out

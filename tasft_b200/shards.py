@@ -176,8 +176,8 @@ def long_context_decode(
     kl = local_kept(kept, lo, hi)
     po = torch.empty(B, Hq, D, dtype=torch.float32, device=q.device)
     pm = torch.empty(B, Hq, 2, dtype=torch.float32, device=q.device)
-    bsa_decode(q, k_local, v_local, local_kv_len(kv_len, lo, hi, block), kl, block,
-               num_splits=num_splits, partials=(po, pm))
+    bsa_decode(q, k_local, v_local, kv_len, kl, block, num_splits=num_splits, partials=(po, pm),
+               kv_offset=lo * block)
     ao, am = gather_partials(po, pm, group)
     return decode_combine(ao, am, q.dtype)
 
@@ -283,8 +283,10 @@ class SplitKVDecoder:
 
         nloc = k_local.shape[2] // self.block
         kl = local if local is not None else local_kept(kept, block_lo, block_lo + nloc)
-        bsa_decode(q, k_local, v_local, local_kv_len(kv_len, block_lo, block_lo + nloc, self.block), kl, self.block,
-                   num_splits=self.num_splits, workspace=self.ws, partials=(self.po, self.pm))
+        # the slab's valid length comes from kv_len and the slab offset inside the kernel (no
+        # per-step tensor ops)
+        bsa_decode(q, k_local, v_local, kv_len, kl, self.block, num_splits=self.num_splits, workspace=self.ws,
+                   partials=(self.po, self.pm), kv_offset=block_lo * self.block)
         if self.peer is not None:
             return self.peer(self.po, self.pm, self.out)
         if self.nccl:
