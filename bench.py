@@ -375,6 +375,7 @@ def bench_epilogue_gate(gate, flush, ws, args, peaks):
             "epilogue_roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_e * 1e-3) / 1e9, 1),
                                   "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                   "frac": round(nbytes / (ms_e * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                                  "traffic": load_traffic().get("epilogue"),
                                   "algorithmic": f"{nbytes / 1e6:.1f} MB (read + write of q, k, v; cos, sin)"},
             "gate_from_means_ms": round(ms_g, 4),
             "what": "qkv_rope_pool (tasft_qkv_rope_pool) on [B, S, H*D] projection outputs, then "
@@ -659,7 +660,7 @@ def run_ours(args):
                  "roofline": {"bound": "hbm", "achieved": round(gbytes / (ms_g * 1e-3) / 1e9, 1),
                               "peak": peaks["hbm_gbs"], "unit": "GB/s",
                               "frac": round(gbytes / (ms_g * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
-                              "traffic": traffic.get("gate_pool"),
+                              "traffic": traffic.get("gate"),
                               "algorithmic": f"{gbytes / 1e6:.1f} MB per step (|Q| + |K|)"}}
 
     # ---------------- projection epilogue + gate from its block means ----------------
@@ -900,6 +901,39 @@ def run_only(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.only == "epilogue":  # qkv_rope_pool on the C2 projection outputs
+        c = CFG
+        g = torch.Generator(device=dev).manual_seed(77)
+        ql = torch.randn(c["B"], c["S"], c["Hq"] * c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+        kl = torch.randn(c["B"], c["S"], c["Hk"] * c["D"], device=dev, dtype=torch.bfloat16, generator=g)
+        vl = torch.randn_like(kl)
+        inv = 1.0 / (10000 ** (torch.arange(0, c["D"], 2, device=dev).float() / c["D"]))
+        emb = torch.cat([torch.outer(torch.arange(c["S"], device=dev).float(), inv)] * 2, -1)
+        cos, sin = emb.cos().bfloat16()[None], emb.sin().bfloat16()[None]
+        for _ in range(args.steps):
+            T.qkv_rope_pool(ql, kl, vl, c["Hq"], c["Hk"], cos, sin, c["block"])
+        torch.cuda.synchronize()
+        print(f"{args.only}: {args.steps} launches ok")
+        return
+    if args.only == "long_decode":  # configs[3] decode on one GPU: wide splits + merge kernel
+        from tasft_b200 import masks as M  # noqa: PLC0415
+
+        lc = LONG
+        g = torch.Generator(device=dev).manual_seed(1234 + 4)
+        ql = torch.randn(lc["B"], lc["Hq"], lc["D"], device=dev, dtype=torch.bfloat16, generator=g)
+        kl = torch.randn(lc["B"], lc["Hk"], lc["L"], lc["D"], device=dev, dtype=torch.bfloat16, generator=g)
+        vl = torch.randn_like(kl)
+        nbl = lc["L"] // lc["block"]
+        kvl = torch.full((lc["B"],), lc["L"], dtype=torch.int32, device=dev)
+        lmask = M.decode_mask(torch.rand(lc["B"], lc["Hk"], nbl, device=dev, generator=g), (kvl + 63) // 64,
+                              lc["density"], nbl)
+        lkept = T.KeptBlocks(*M.lists_from_mask(lmask))
+        lws = T.DecodeWorkspace(lc["B"], lc["Hq"], lc["Hk"], lc["D"], 64, dev)
+        for _ in range(args.steps):
+            T.bsa_decode(ql, kl, vl, kvl, lkept, lc["block"], workspace=lws)
+        torch.cuda.synchronize()
+        print(f"{args.only}: {args.steps} launches ok")
+        return
     if args.only in ("decode", "paged"):
         qd, kc, vc, kv_len, kept = make_decode_inputs(1237, dev)
         splits = T.decode.default_splits(DEC["B"], DEC["Hk"], float(kept.cnt.float().mean().item()))
@@ -943,7 +977,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-triton", action="store_true", help="skip timing the reference Triton kernel")
-    ap.add_argument("--only", choices=["prefill", "decode", "paged", "gate", "target"],
+    ap.add_argument("--only", choices=["prefill", "decode", "paged", "gate", "target", "epilogue", "long_decode"],
                     help="profiling driver: run `--steps` launches of one kernel family, print nothing else")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
