@@ -807,7 +807,8 @@ def run_ours(args):
         dec = SH.SplitKVDecoder(lc["B"], lc["Hq"], lc["Hk"], lc["D"], dev, exchange="peer")
         lloc = dec.local(lkept, lo, hi - lo)
         lstep = graphed(lambda: dec(ql, kl_loc, vl_loc, kvl, lkept, lo, local=lloc))
-        ltiming = "CUDA graph replay (local split decode + peer-memory merge kernel)"
+        ltiming = ("CUDA graph replay (local split decode whose merge kernel pushes the rank's rows to every "
+                   "rank over peer memory and merges them: tasft_bsa_decode_peer_fwd)")
         # the NCCL all-gather + combine path, eager, for comparison
         dec_n = SH.SplitKVDecoder(lc["B"], lc["Hq"], lc["Hk"], lc["D"], dev, exchange="nccl")
         t_n = time_steps(lambda: dec_n(ql, kl_loc, vl_loc, kvl, lkept, lo, local=lloc), args.steps, args.warmup,
@@ -818,7 +819,8 @@ def run_ours(args):
                                                          partials=(dec.po, dec.pm), kv_offset=lo * lc["block"])),
                            args.steps, args.warmup, flush, ws)
         long_extra["ms_local_decode_only"] = round(max_over_ranks(statistics.mean(t_loc), ws), 4)
-        # and the peer-memory merge alone (every rank replays it, so the ranks still meet)
+        # and the stand-alone peer-memory merge kernel (tasft_peer_combine) alone, for comparison
+        # (every rank replays it, so the ranks still meet)
         t_mrg = time_steps(graphed(lambda: dec.peer(dec.po, dec.pm, dec.out)), args.steps, args.warmup, flush, ws)
         long_extra["ms_merge_only"] = round(max_over_ranks(statistics.mean(t_mrg), ws), 4)
     else:

@@ -321,6 +321,25 @@ typedef struct {
   int32_t* err;           /* optional device error word */
 } tasft_peer_combine_args;
 TASFT_API int64_t tasft_peer_mailbox_bytes(int32_t world, int64_t rows, int32_t D);
+
+/* Split-KV decode with the cross-GPU merge fused in: one call runs this rank's decode over its
+ * slab of the cache, and the kernel that merges the rank's splits also pushes the rank's
+ * (o, m, l) rows straight into every rank's mailbox (plain stores through the IPC mappings,
+ * a release flag per row), waits (bounded by timeout_ns; TASFT_DEVERR_TIMEOUT into
+ * args->err on expiry) for every rank's rows in its own mailbox and writes the merged
+ * output to args->out. Replaces tasft_bsa_decode_fwd (with part_o / part_ml) followed by
+ * tasft_peer_combine; same mailboxes (tasft_peer_mailbox_bytes, tasft_peer_alloc,
+ * tasft_ipc_*) and epoch, so the two may be mixed in one sequence of calls that every rank
+ * makes alike. bf16 / f16, block 64, D 64 / 128, group <= 8, world <= 8; needs a workspace
+ * (at least 2 splits). No counterpart in the reference (it has no sparse decode). */
+typedef struct {
+  void* const* mailboxes; /* device array [world] of device pointers, as in tasft_peer_combine_args */
+  uint32_t* epoch;        /* device scalar of this rank */
+  int32_t world, rank;
+  uint64_t timeout_ns;
+} tasft_decode_peer_args;
+TASFT_API int tasft_bsa_decode_peer_fwd(const tasft_decode_args* args, const tasft_decode_peer_args* peer,
+                                        tasft_stream_t stream);
 TASFT_API int tasft_peer_alloc(int64_t bytes, void** ptr);
 TASFT_API int tasft_peer_free(void* ptr);
 TASFT_API int tasft_ipc_handle(void* ptr, uint8_t* handle64);

@@ -119,6 +119,10 @@ class CombineArgs(C.Structure):
     ]
 
 
+class DecodePeerArgs(C.Structure):
+    _fields_ = [("mailboxes", vp), ("epoch", vp), ("world", C.c_int32), ("rank", C.c_int32), ("timeout_ns", C.c_uint64)]
+
+
 class PeerCombineArgs(C.Structure):
     _fields_ = [
         ("part_o", vp), ("part_ml", vp), ("rows", C.c_int64), ("D", C.c_int32), ("world", C.c_int32),
@@ -189,6 +193,7 @@ SIGNATURES = {
     "tasft_ipc_open": ([C.c_char_p, C.POINTER(vp)], C.c_int),
     "tasft_ipc_close": ([vp], C.c_int),
     "tasft_peer_combine": ([C.POINTER(PeerCombineArgs), vp], C.c_int),
+    "tasft_bsa_decode_peer_fwd": ([C.POINTER(DecodeArgs), C.POINTER(DecodePeerArgs), vp], C.c_int),
     "tasft_gate_target_workspace_size": ([C.c_int32] * 4, C.c_int64),
     "tasft_gate_target_fwd": ([C.POINTER(TargetArgs), vp], C.c_int),
     "tasft_scores_target_workspace_size": ([C.c_int32] * 5, C.c_int64),

@@ -372,6 +372,27 @@ extern "C" int tasft_bsa_decode_fwd(const tasft_decode_args* ap, tasft_stream_t 
   return decode_run(a, ws, nsplit, st);
 }
 
+extern "C" int tasft_bsa_decode_peer_fwd(const tasft_decode_args* ap, const tasft_decode_peer_args* pp,
+                                         tasft_stream_t stream) {
+  if (!ap || !pp) return TASFT_ERR_INVALID_ARG;
+  const tasft_decode_args& a = *ap;
+  int rc = decode_check_args(a);
+  if (rc != TASFT_OK) return rc;
+  if (!a.out || !pp->mailboxes || !pp->epoch) return TASFT_ERR_INVALID_ARG;
+  if (pp->world <= 0 || pp->world > 8 || pp->rank < 0 || pp->rank >= pp->world) return TASFT_ERR_INVALID_ARG;
+  if (!decode_mma_ok(a)) return TASFT_ERR_UNSUPPORTED;
+  int nsplit = decode_pick_splits(a);
+  if (nsplit < 2) nsplit = 2;  // the exchange runs in the separate merge kernel
+  if (!a.workspace) return TASFT_ERR_WORKSPACE;
+  DecodeWs ws{nullptr, nullptr, 0};
+  rc = decode_ws_from(a, nsplit, &ws);
+  if (rc != TASFT_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = decode_clear_tickets(a, ws, st);
+  if (rc != TASFT_OK) return rc;
+  return decode_mma(a, ws, nsplit, st, PeerMode{pp->mailboxes, pp->epoch, pp->world, pp->rank, pp->timeout_ns});
+}
+
 extern "C" int tasft_bsa_decode_combine(const tasft_combine_args* ap, tasft_stream_t stream) {
   if (!ap || !ap->part_o || !ap->part_ml || !ap->out || ap->G <= 0 || ap->rows <= 0 || ap->D <= 0)
     return TASFT_ERR_INVALID_ARG;

@@ -84,7 +84,15 @@ __device__ void decode_finish(const tasft_decode_args& a, const DecodeWs& ws, in
 
 // whether the tensor-core decode takes these arguments (bf16/f16, block 64, D 64/128, group <= 8)
 bool decode_mma_ok(const tasft_decode_args& a);
-int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st);
+// Cross-GPU exchange done by the wide-split merge kernel (world == 0: off)
+struct PeerMode {
+  void* const* mailboxes;
+  uint32_t* epoch;
+  int world, rank;
+  uint64_t timeout_ns;
+};
+int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st,
+               const PeerMode& pm = PeerMode{nullptr, nullptr, 0, 0, 0});
 // Paged-cache variant (k_cache / v_cache are page pools, see tasft_bsa_decode_paged_fwd).
 int decode_mma_paged(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const int32_t* table, int max_pages,
                      int page_size, int num_pages, cudaStream_t st);

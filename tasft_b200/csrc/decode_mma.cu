@@ -22,6 +22,7 @@
 //   through an atomic ticket: the last split to finish merges all partials.
 #include "decode.cuh"
 #include "tc.cuh"
+#include "peer.cuh"
 
 namespace tasft {
 namespace {
@@ -495,7 +496,7 @@ constexpr int kMergeThreads = 128;
 
 template <int D, bool kF16>
 __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const tasft_decode_args a, const DecodeWs ws,
-                                                                      const int nsplit) {
+                                                                      const int nsplit, const PeerMode pm) {
   using T = typename std::conditional<kF16, __half, __nv_bfloat16>::type;
   constexpr int kW = kMergeThreads / 32;
   constexpr int DP = D / 64;  // float2 per lane
@@ -574,22 +575,99 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const tasft
   }
   const float inv = dt > 0.f ? 1.f / dt : 0.f;
   const int b = (int)(row / a.Hq), hq = (int)(row % a.Hq);
-  for (int d = threadIdx.x; d < D; d += kMergeThreads) {
-    float t = 0.f;
+  if (pm.world == 0) {
+    for (int d = threadIdx.x; d < D; d += kMergeThreads) {
+      float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < kW; ++w) t += scw[w] * s_num[w][d];
-    const float ov = t * inv;
-    if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(ov);
-    if (a.part_o) a.part_o[row * D + d] = ov;
+      for (int w = 0; w < kW; ++w) t += scw[w] * s_num[w][d];
+      const float ov = t * inv;
+      if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(ov);
+      if (a.part_o) a.part_o[row * D + d] = ov;
+    }
+    if (a.part_ml && threadIdx.x == 0) {
+      a.part_ml[row * 2] = mt;
+      a.part_ml[row * 2 + 1] = dt;
+    }
+    return;
   }
-  if (a.part_ml && threadIdx.x == 0) {
-    a.part_ml[row * 2] = mt;
-    a.part_ml[row * 2 + 1] = dt;
+  // ---- cross-GPU exchange of this row (tasft_bsa_decode_peer_fwd; mailbox layout in
+  //      peer.cuh): push (o, m, l) into slot [parity][rank][row] of every rank's mailbox,
+  //      fence, one release flag per mailbox; wait for every rank's flag of this row in this
+  //      rank's mailbox; merge as tasft_bsa_decode_combine does ----
+  const int world = pm.world, rank = pm.rank;
+  const int64_t rows = (int64_t)a.B * a.Hq;
+  const uint32_t e = *pm.epoch + 1u;
+  const int par = (int)(e & 1u);
+  const int64_t poff = peer_part_off(world, rows);
+  const int64_t fl_row = peer_flags_bytes(world) / 4;  // uint32 offset of the row flags
+  for (int p = 0; p < world; ++p) {
+    float* dst = reinterpret_cast<float*>(pm.mailboxes[p]) + poff + (((int64_t)par * world + rank) * rows + row) * (D + 2);
+    for (int d = threadIdx.x; d < D; d += kMergeThreads) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kW; ++w) t += scw[w] * s_num[w][d];
+      dst[d] = t * inv;
+    }
+    if (threadIdx.x == 0) {
+      dst[D] = mt;
+      dst[D + 1] = dt;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int p = 0; p < world; ++p)
+      st_release_sys(reinterpret_cast<uint32_t*>(pm.mailboxes[p]) + fl_row + (int64_t)rank * rows + row, e);
+  __shared__ int s_timeout;
+  if (threadIdx.x == 0) s_timeout = 0;
+  __syncthreads();
+  const uint32_t* own = reinterpret_cast<const uint32_t*>(pm.mailboxes[rank]);
+  if (threadIdx.x < world) {
+    const uint32_t* flag = own + fl_row + (int64_t)threadIdx.x * rows + row;
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t)(ld_acquire_sys(flag) - e) < 0) {
+      if (globaltimer_ns() - t0 > pm.timeout_ns) {
+        atomicOr(&s_timeout, 1);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (s_timeout && threadIdx.x == 0) set_err(a.err, TASFT_DEVERR_TIMEOUT);
+  const float* box = reinterpret_cast<const float*>(pm.mailboxes[rank]) + poff;
+  float gmax = -INFINITY;
+  for (int g = 0; g < world; ++g) {
+    const float* pr = box + (((int64_t)par * world + g) * rows + row) * (D + 2);
+    if (pr[D + 1] > 0.f) gmax = fmaxf(gmax, pr[D]);
+  }
+  for (int d = threadIdx.x; d < D; d += kMergeThreads) {
+    float num = 0.f, den = 0.f;
+    for (int g = 0; g < world; ++g) {
+      const float* pr = box + (((int64_t)par * world + g) * rows + row) * (D + 2);
+      const float l = pr[D + 1];
+      if (l > 0.f) {
+        const float w = l * __expf(pr[D] - gmax);
+        num = fmaf(w, pr[d], num);
+        den += w;
+      }
+    }
+    if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(den > 0.f ? num / den : 0.f);
+  }
+  // the last row's CTA to finish advances the epoch (every CTA read it on entry)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* done = reinterpret_cast<int*>(pm.mailboxes[rank]) + world;  // call flags' spare word
+    if (atomicAdd(done, 1) == (int)gridDim.x - 1) {
+      *done = 0;
+      __threadfence();
+      *pm.epoch = e;
+    }
   }
 }
 
 template <int D, bool kF16, bool kPaged>
-int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const PagedInfo& pg, cudaStream_t st) {
+int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const PagedInfo& pg, cudaStream_t st,
+               const PeerMode& pm) {
   CUtensorMap mk, mv;
   bool maps;
   if constexpr (kPaged) {
@@ -621,7 +699,7 @@ int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const
   if (debug_enabled())
     debug_log("decode_mma D=%d f16=%d paged=%d grid=%lld smem=%d splits=%d", D, (int)kF16, (int)kPaged,
               (long long)grid, smem, nsplit);
-  const int inline_merge = nsplit <= kInlineMergeMaxSplits;
+  const int inline_merge = nsplit <= kInlineMergeMaxSplits && pm.world == 0;
   kern<<<(unsigned)grid, kThreadsM, smem, st>>>(mk, mv, a, ws, nsplit, pg, inline_merge);
   count_launch();
   if (inline_merge) return launch_status();
@@ -636,7 +714,7 @@ int launch_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, decode_merge_kernel<D, kF16>, a, ws, nsplit) != cudaSuccess) return launch_status();
+  if (cudaLaunchKernelEx(&cfg, decode_merge_kernel<D, kF16>, a, ws, nsplit, pm) != cudaSuccess) return launch_status();
   count_launch();
   return launch_status();
 }
@@ -651,25 +729,29 @@ bool mma_ok(const tasft_decode_args& a) {
 }
 
 template <bool kPaged>
-int dispatch(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const PagedInfo& pg, cudaStream_t st) {
+int dispatch(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const PagedInfo& pg, cudaStream_t st,
+             const PeerMode& pm) {
   if (!mma_ok(a)) return TASFT_ERR_UNSUPPORTED;
   const bool f16 = a.dtype == TASFT_F16;
   if (a.D == 128)
-    return f16 ? launch_mma<128, true, kPaged>(a, ws, nsplit, pg, st) : launch_mma<128, false, kPaged>(a, ws, nsplit, pg, st);
-  return f16 ? launch_mma<64, true, kPaged>(a, ws, nsplit, pg, st) : launch_mma<64, false, kPaged>(a, ws, nsplit, pg, st);
+    return f16 ? launch_mma<128, true, kPaged>(a, ws, nsplit, pg, st, pm)
+               : launch_mma<128, false, kPaged>(a, ws, nsplit, pg, st, pm);
+  return f16 ? launch_mma<64, true, kPaged>(a, ws, nsplit, pg, st, pm)
+             : launch_mma<64, false, kPaged>(a, ws, nsplit, pg, st, pm);
 }
 
 }  // namespace
 
 bool decode_mma_ok(const tasft_decode_args& a) { return mma_ok(a); }
 
-int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st) {
-  return dispatch<false>(a, ws, nsplit, PagedInfo{nullptr, 0, 0, 0}, st);
+int decode_mma(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, cudaStream_t st, const PeerMode& pm) {
+  return dispatch<false>(a, ws, nsplit, PagedInfo{nullptr, 0, 0, 0}, st, pm);
 }
 
 int decode_mma_paged(const tasft_decode_args& a, const DecodeWs& ws, int nsplit, const int32_t* table, int max_pages,
                      int page_size, int num_pages, cudaStream_t st) {
-  return dispatch<true>(a, ws, nsplit, PagedInfo{table, max_pages, page_size, num_pages}, st);
+  return dispatch<true>(a, ws, nsplit, PagedInfo{table, max_pages, page_size, num_pages}, st,
+                       PeerMode{nullptr, nullptr, 0, 0, 0});
 }
 
 }  // namespace tasft

@@ -7,32 +7,22 @@
 // ranks in its own mailbox, and merges the partials (log-sum-exp). One small kernel per
 // step, no host involvement, so the whole decode step can be replayed from a CUDA graph.
 //
-// Mailbox of a rank (tasft_peer_mailbox_bytes): flags [world] uint32 (padded to 256 B),
-// then partials [2 parity][world][rows][D + 2] fp32. A call's epoch e = (*epoch) + 1
-// selects parity e & 1: a rank can be at most one call ahead of another (it waits for all
-// flags of its own call), so the other parity is never overwritten while it is read.
+// Mailbox of a rank: see peer.cuh (this kernel uses the call flags and the partials). A
+// call's epoch e = (*epoch) + 1 selects parity e & 1: a rank can be at most one call ahead
+// of another (it waits for all flags of its own call), so the other parity is never
+// overwritten while it is read.
 // No TMA, no multicast, no multimem: plain ld/st to peer memory.
 #include <cuda_runtime.h>
 
 #include <cstring>
 
-#include "common.cuh"
+#include "peer.cuh"
 
 namespace tasft {
 namespace {
 
 constexpr int kPeerThreads = 512;
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__host__ __device__ inline int64_t flags_bytes(int world) { return ((int64_t)world * 4 + 255) / 256 * 256; }
 
 constexpr int kRowChunk = 128;  // rows whose merge weights sit in shared memory at once
 constexpr int kMaxWorld = 8;
@@ -44,7 +34,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_combine_kernel(tasft_peer_c
   const int64_t slab = rows * (D + 2);  // floats of one rank's partial
   const uint32_t e = *a.epoch + 1u;
   const int par = (int)(e & 1u);
-  const int64_t foff = flags_bytes(world) / 4;  // float offset of the partials
+  const int64_t foff = peer_part_off(world, rows);  // float offset of the partials
   // 1. push this rank's (o | m, l) rows into slot [par][rank] of every mailbox, 8 bytes per
   //    store (a row is D + 2 floats, D even: rows stay 8-byte aligned)
   const int64_t rp = (D + 2) / 2;  // float2 per mailbox row
@@ -128,7 +118,7 @@ using namespace tasft;
 
 extern "C" int64_t tasft_peer_mailbox_bytes(int32_t world, int64_t rows, int32_t D) {
   if (world <= 0 || rows <= 0 || D <= 0) return -1;
-  return flags_bytes(world) + (int64_t)2 * world * rows * (D + 2) * 4;
+  return peer_mailbox_bytes(world, rows, D);
 }
 
 extern "C" int tasft_peer_alloc(int64_t bytes, void** ptr) {

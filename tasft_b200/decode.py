@@ -117,6 +117,38 @@ def bsa_decode(
     return out
 
 
+def bsa_decode_peer(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    kv_len: torch.Tensor,
+    kept: KeptBlocks,
+    peer,
+    block: int = 64,
+    *,
+    workspace: DecodeWorkspace,
+    out: torch.Tensor,
+    num_splits: int = 0,
+    kv_offset: int = 0,
+) -> torch.Tensor:
+    """One rank's share of a split-KV decode with the cross-GPU merge fused into its merge
+    kernel (``tasft_bsa_decode_peer_fwd``): decodes this rank's slab (``kv_offset`` as in
+    :func:`bsa_decode`), pushes the rank's ``(o, m, l)`` rows into every rank's mailbox of
+    ``peer`` (a :class:`tasft_b200.shards.PeerExchange`) and writes the merge of all ranks
+    into ``out``. Every rank makes the same calls; a wait that runs out sets ``peer.err``."""
+    L.require_cuda(q, k_cache, v_cache, kv_len)
+    B, Hq, D = q.shape
+    Hk, Lc = k_cache.shape[1], k_cache.shape[2]
+    q = q.contiguous()
+    args, num_splits, _keep = _decode_args(q, k_cache.contiguous(), v_cache.contiguous(), kv_len, kept, block, Lc, Hk,
+                                           num_splits, workspace, out, None, peer.err, kv_offset)
+    pa = L.DecodePeerArgs(mailboxes=peer.table.data_ptr(), epoch=peer.epoch.data_ptr(), world=peer.world,
+                          rank=peer.rank, timeout_ns=peer.timeout_ns)
+    L.check(L.lib().tasft_bsa_decode_peer_fwd(args, pa, L.stream_ptr(q.device)), "tasft_bsa_decode_peer_fwd",
+            shape=[B, Hq, Hk, Lc, D], splits=num_splits)
+    return out
+
+
 def bsa_decode_paged(
     q: torch.Tensor,
     k_pages: torch.Tensor,
@@ -177,4 +209,4 @@ def decode_combine(part_o: torch.Tensor, part_ml: torch.Tensor, out_dtype=torch.
     return out
 
 
-__all__ = ["DecodeWorkspace", "bsa_decode", "bsa_decode_paged", "decode_combine", "default_splits"]
+__all__ = ["DecodeWorkspace", "bsa_decode", "bsa_decode_paged", "bsa_decode_peer", "decode_combine", "default_splits"]

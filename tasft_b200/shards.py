@@ -251,7 +251,7 @@ class SplitKVDecoder:
     caller pass the rank's rebased kept lists when they did not change since the last step."""
 
     def __init__(self, B: int, Hq: int, Hk: int, D: int, device, group=None, block: int = 64,
-                 num_splits: int = 0, exchange: str = "nccl", out_dtype=torch.bfloat16) -> None:
+                 num_splits: int = 0, exchange: str = "nccl", out_dtype=torch.bfloat16, fused: bool = True) -> None:
         import torch.distributed as dist  # noqa: PLC0415
 
         from tasft_b200.decode import DecodeWorkspace  # noqa: PLC0415
@@ -259,6 +259,12 @@ class SplitKVDecoder:
         if exchange not in ("nccl", "peer"):
             raise ValueError(f"exchange must be 'nccl' or 'peer', got {exchange!r}")
         self.group, self.block, self.num_splits = group, block, num_splits
+        # "peer" + fused: the exchange runs inside the decode's merge kernel
+        # (tasft_bsa_decode_peer_fwd) where that kernel applies (bf16/f16, block 64, D 64/128,
+        # up to 8 q-heads per kv-head); otherwise decode, then the separate merge kernel
+        from tasft_b200.decode import max_splits_for  # noqa: PLC0415
+
+        self.fused = fused and exchange == "peer" and max_splits_for(out_dtype, block, D, Hq // Hk) == 64
         self.world = dist.get_world_size(group)
         self.nccl = dist.get_backend(group) == "nccl"
         # "peer": partials merged over peer memory by one kernel (graph-capturable step)
@@ -279,10 +285,14 @@ class SplitKVDecoder:
                  local: KeptBlocks | None = None) -> torch.Tensor:
         import torch.distributed as dist  # noqa: PLC0415
 
-        from tasft_b200.decode import bsa_decode, decode_combine  # noqa: PLC0415
+        from tasft_b200.decode import bsa_decode, bsa_decode_peer, decode_combine  # noqa: PLC0415
 
         nloc = k_local.shape[2] // self.block
         kl = local if local is not None else local_kept(kept, block_lo, block_lo + nloc)
+        if self.peer is not None and self.fused:
+            # the decode's own merge kernel pushes this rank's rows to every rank and merges
+            return bsa_decode_peer(q, k_local, v_local, kv_len, kl, self.peer, self.block, workspace=self.ws,
+                                   out=self.out, num_splits=self.num_splits, kv_offset=block_lo * self.block)
         # the slab's valid length comes from kv_len and the slab offset inside the kernel (no
         # per-step tensor ops)
         bsa_decode(q, k_local, v_local, kv_len, kl, self.block, num_splits=self.num_splits, workspace=self.ws,

@@ -1,4 +1,5 @@
-"""Split-KV decode partials merged over peer memory (tasft_peer_combine).
+"""Split-KV decode partials merged over peer memory (tasft_peer_combine, and the decode
+whose merge kernel exchanges itself, tasft_bsa_decode_peer_fwd).
 
 On one GPU the other rank is emulated by the host: its partial and its flag are written
 into this rank's mailbox before the call (no kernel ever waits for another kernel on the
@@ -31,8 +32,19 @@ def _mailbox(world, rows, D):
     return torch.zeros(nbytes // 4, dtype=torch.int32, device=DEV)
 
 
+def _part_off(world, rows):
+    """Float offset of the partials in a mailbox: call flags (world + 1 words) and row flags
+    (world x rows words), each padded to 256 bytes."""
+    return (((world + 1) * 4 + 255) // 256 * 256 + (world * rows * 4 + 255) // 256 * 256) // 4
+
+
+def _rowflags(box, world, rows):
+    base = ((world + 1) * 4 + 255) // 256 * 256 // 4
+    return box[base: base + world * rows].view(world, rows)
+
+
 def _slot(box, world, rows, D, par, r):
-    foff = ((world * 4 + 255) // 256 * 256) // 4
+    foff = _part_off(world, rows)
     slab = rows * (D + 2)
     return box.view(torch.float32)[foff + (par * world + r) * slab: foff + (par * world + r + 1) * slab].view(rows, D + 2)
 
@@ -89,6 +101,83 @@ def test_missing_peer_times_out_with_error_bit():
     out = torch.empty(rows, D, dtype=torch.bfloat16, device=DEV)
     _call(boxes, 0, po, pm, out, epoch, err, timeout_ns=int(5e7))  # flag of rank 1 never raised
     assert int(err.item()) & L.DEVERR_TIMEOUT
+
+
+class _Peer:
+    """The fields of shards.PeerExchange that bsa_decode_peer reads, over local mailboxes."""
+
+    def __init__(self, boxes, rank, timeout_ns):
+        self.table = torch.tensor([b.data_ptr() for b in boxes], dtype=torch.int64, device=DEV)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=DEV)
+        self.err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        self.world, self.rank, self.timeout_ns = len(boxes), rank, timeout_ns
+
+
+def _slab_case():
+    g = torch.Generator(device=DEV).manual_seed(8)
+    B, Hq, Hk, Lc, D = 1, 28, 4, 8192, 128
+    q = torch.randn(B, Hq, D, device=DEV, generator=g).bfloat16()
+    kc = torch.randn(B, Hk, Lc, D, device=DEV, generator=g).bfloat16()
+    vc = torch.randn(B, Hk, Lc, D, device=DEV, generator=g).bfloat16()
+    kv_len = torch.full((B,), Lc - 37, dtype=torch.int32, device=DEV)
+    nb = Lc // 64
+    mask = M.decode_mask(torch.rand(B, Hk, nb, device=DEV, generator=g), (kv_len + 63) // 64, 0.15, nb)
+    return q, kc, vc, kv_len, T.KeptBlocks(*M.lists_from_mask(mask)), nb
+
+
+def test_fused_decode_exchange_emulated_twice():
+    """Rank 0 of 2 on one GPU: rank 1's rows (its own slab decoded with partials) and row
+    flags are written into rank 0's mailbox by the host; the fused call must agree with the
+    NCCL path's combine of the two slabs' partials and with a one-rank decode of the whole
+    cache, leave its own rows and flags in rank 1's mailbox, and advance the epoch."""
+    q, kc, vc, kv_len, kept, nb = _slab_case()
+    B, Hq, D = q.shape
+    rows, world, half = B * Hq, 2, nb // 2
+    boxes = [_mailbox(world, rows, D), _mailbox(world, rows, D)]
+    peer = _Peer(boxes, 0, int(2e8))
+    ws = T.DecodeWorkspace(B, Hq, 4, D, 64, DEV)
+    slabs = [(kc[:, :, :half * 64].contiguous(), vc[:, :, :half * 64].contiguous(), 0),
+             (kc[:, :, half * 64:].contiguous(), vc[:, :, half * 64:].contiguous(), half)]
+    parts = []
+    for k_s, v_s, lo in slabs:
+        kl = SH.local_kept(kept, lo, lo + half)
+        po = torch.empty(B, Hq, D, device=DEV)
+        pm = torch.empty(B, Hq, 2, device=DEV)
+        T.bsa_decode(q, k_s, v_s, kv_len, kl, 64, workspace=ws, partials=(po, pm), kv_offset=lo * 64)
+        parts.append((po.view(rows, D), pm.view(rows, 2), kl))
+    full = T.bsa_decode(q, kc, vc, kv_len, kept, 64)
+    for call in (1, 2):
+        par = call & 1
+        _slot(boxes[0], world, rows, D, par, 1).copy_(torch.cat([parts[1][0], parts[1][1]], -1))
+        _rowflags(boxes[0], world, rows)[1].fill_(call)
+        out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=DEV)
+        T.decode.bsa_decode_peer(q, slabs[0][0], slabs[0][1], kv_len, parts[0][2], peer, 64, workspace=ws, out=out)
+        torch.cuda.synchronize()
+        assert int(peer.err.item()) == 0 and int(peer.epoch.item()) == call
+        ref = T.decode_combine(torch.stack([parts[0][0], parts[1][0]]).view(2, B, Hq, D),
+                               torch.stack([parts[0][1], parts[1][1]]).view(2, B, Hq, 2), torch.bfloat16)
+        # this rank's rows come from the separate merge kernel, the reference partials from the
+        # in-kernel merge (16 splits): same maths, fp32 summation orders differ
+        assert (out.float() - ref.float()).abs().max().item() <= 1e-2
+        assert (out.float() - full.float()).abs().max().item() <= 2e-2
+        pushed = _slot(boxes[1], world, rows, D, par, 0)
+        own = torch.cat([parts[0][0], parts[0][1]], -1)
+        assert torch.allclose(pushed, own, rtol=1e-4, atol=1e-5)
+        assert bool((_rowflags(boxes[1], world, rows)[0] == call).all())
+
+
+def test_fused_decode_exchange_missing_peer_times_out():
+    q, kc, vc, kv_len, kept, nb = _slab_case()
+    B, Hq, D = q.shape
+    boxes = [_mailbox(2, B * Hq, D), _mailbox(2, B * Hq, D)]
+    peer = _Peer(boxes, 0, int(5e7))  # rank 1's row flags are never raised
+    ws = T.DecodeWorkspace(B, Hq, 4, D, 64, DEV)
+    half = nb // 2
+    out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=DEV)
+    T.decode.bsa_decode_peer(q, kc[:, :, :half * 64].contiguous(), vc[:, :, :half * 64].contiguous(), kv_len,
+                             SH.local_kept(kept, 0, half), peer, 64, workspace=ws, out=out)
+    torch.cuda.synchronize()
+    assert int(peer.err.item()) & L.DEVERR_TIMEOUT
 
 
 def _inputs(dev):
