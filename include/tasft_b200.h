@@ -324,10 +324,10 @@ TASFT_API int64_t tasft_peer_mailbox_bytes(int32_t world, int64_t rows, int32_t 
 
 /* Split-KV decode with the cross-GPU merge fused in: one call runs this rank's decode over its
  * slab of the cache, and the kernel that merges the rank's splits also pushes the rank's
- * (o, m, l) rows straight into every rank's mailbox (plain stores through the IPC mappings,
- * a release flag per row), waits (bounded by timeout_ns; TASFT_DEVERR_TIMEOUT into
- * args->err on expiry) for every rank's rows in its own mailbox and writes the merged
- * output to args->out. Replaces tasft_bsa_decode_fwd (with part_o / part_ml) followed by
+ * (o, m, l) rows straight into every rank's mailbox (plain 8-byte stores through the IPC
+ * mappings, each word carrying the call's epoch beside its value, so no fence or flag),
+ * waits (bounded by timeout_ns; TASFT_DEVERR_TIMEOUT into args->err on expiry) for every
+ * rank's rows in its own mailbox and writes the merged output to args->out. Replaces tasft_bsa_decode_fwd (with part_o / part_ml) followed by
  * tasft_peer_combine; same mailboxes (tasft_peer_mailbox_bytes, tasft_peer_alloc,
  * tasft_ipc_*) and epoch, so the two may be mixed in one sequence of calls that every rank
  * makes alike. bf16 / f16, block 64, D 64 / 128, group <= 8, world <= 8; needs a workspace

@@ -493,6 +493,7 @@ __global__ void __launch_bounds__(kThreadsM, kCtasPerSm)
 // trip to L2 per 64 splits. Same maths as the in-kernel merge:
 // o = sum_s l_s e^(m_s - m) o_s / sum_s l_s e^(m_s - m).
 constexpr int kMergeThreads = 128;
+constexpr int kMaxPeerWorld = 8;  // ranks of one NVLink node (tasft_bsa_decode_peer_fwd checks)
 
 template <int D, bool kF16>
 __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const tasft_decode_args a, const DecodeWs ws,
@@ -591,68 +592,69 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const tasft
     return;
   }
   // ---- cross-GPU exchange of this row (tasft_bsa_decode_peer_fwd; mailbox layout in
-  //      peer.cuh): push (o, m, l) into slot [parity][rank][row] of every rank's mailbox,
-  //      fence, one release flag per mailbox; wait for every rank's flag of this row in this
-  //      rank's mailbox; merge as tasft_bsa_decode_combine does ----
+  //      peer.cuh): every value of the row's (o, m, l) goes to slot [parity][rank][row] of
+  //      every rank's mailbox as one 8-byte word (value | epoch << 32); then each thread
+  //      spins (bounded) on the words it needs in this rank's mailbox until they carry this
+  //      call's epoch, and merges as tasft_bsa_decode_combine does. No fence, no flag: a word
+  //      is published by the store that writes it ----
   const int world = pm.world, rank = pm.rank;
   const int64_t rows = (int64_t)a.B * a.Hq;
   const uint32_t e = *pm.epoch + 1u;
   const int par = (int)(e & 1u);
-  const int64_t poff = peer_part_off(world, rows);
-  const int64_t fl_row = peer_flags_bytes(world) / 4;  // uint32 offset of the row flags
-  for (int p = 0; p < world; ++p) {
-    float* dst = reinterpret_cast<float*>(pm.mailboxes[p]) + poff + (((int64_t)par * world + rank) * rows + row) * (D + 2);
-    for (int d = threadIdx.x; d < D; d += kMergeThreads) {
+  const int64_t woff = peer_word_off(world);
+  const uint64_t tag = (uint64_t)e << 32;
+  for (int d = threadIdx.x; d < D + 2; d += kMergeThreads) {
+    float v;
+    if (d < D) {
       float t = 0.f;
 #pragma unroll
       for (int w = 0; w < kW; ++w) t += scw[w] * s_num[w][d];
-      dst[d] = t * inv;
+      v = t * inv;
+    } else {
+      v = d == D ? mt : dt;
     }
-    if (threadIdx.x == 0) {
-      dst[D] = mt;
-      dst[D + 1] = dt;
-    }
-  }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0)
+    const uint64_t word = tag | __float_as_uint(v);
     for (int p = 0; p < world; ++p)
-      st_release_sys(reinterpret_cast<uint32_t*>(pm.mailboxes[p]) + fl_row + (int64_t)rank * rows + row, e);
-  __shared__ int s_timeout;
-  if (threadIdx.x == 0) s_timeout = 0;
-  __syncthreads();
-  const uint32_t* own = reinterpret_cast<const uint32_t*>(pm.mailboxes[rank]);
-  if (threadIdx.x < world) {
-    const uint32_t* flag = own + fl_row + (int64_t)threadIdx.x * rows + row;
-    const uint64_t t0 = globaltimer_ns();
-    while ((int32_t)(ld_acquire_sys(flag) - e) < 0) {
-      if (globaltimer_ns() - t0 > pm.timeout_ns) {
-        atomicOr(&s_timeout, 1);
-        break;
-      }
-    }
+      st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(pm.mailboxes[p]) + woff +
+                             (((int64_t)par * world + rank) * rows + row) * (D + 2) + d,
+                         word);
   }
-  __syncthreads();
-  if (s_timeout && threadIdx.x == 0) set_err(a.err, TASFT_DEVERR_TIMEOUT);
-  const float* box = reinterpret_cast<const float*>(pm.mailboxes[rank]) + poff;
+  const uint64_t* box = reinterpret_cast<const uint64_t*>(pm.mailboxes[rank]) + woff;
+  const uint64_t t0 = globaltimer_ns();
+  bool timed_out = false;
+  // a word of this call, spinning until it arrives (0 after the bound)
+  auto fetch = [&](int g, int d) -> float {
+    const uint64_t* src = box + (((int64_t)par * world + g) * rows + row) * (D + 2) + d;
+    uint64_t v = ld_relaxed_sys_u64(src);
+    while ((uint32_t)(v >> 32) != e) {
+      if (timed_out || globaltimer_ns() - t0 > pm.timeout_ns) {
+        timed_out = true;
+        return 0.f;
+      }
+      v = ld_relaxed_sys_u64(src);
+    }
+    return __uint_as_float((uint32_t)v);
+  };
+  float gm[kMaxPeerWorld], gl[kMaxPeerWorld];
   float gmax = -INFINITY;
   for (int g = 0; g < world; ++g) {
-    const float* pr = box + (((int64_t)par * world + g) * rows + row) * (D + 2);
-    if (pr[D + 1] > 0.f) gmax = fmaxf(gmax, pr[D]);
+    gm[g] = fetch(g, D);
+    gl[g] = fetch(g, D + 1);
+    if (gl[g] > 0.f) gmax = fmaxf(gmax, gm[g]);
   }
   for (int d = threadIdx.x; d < D; d += kMergeThreads) {
     float num = 0.f, den = 0.f;
     for (int g = 0; g < world; ++g) {
-      const float* pr = box + (((int64_t)par * world + g) * rows + row) * (D + 2);
-      const float l = pr[D + 1];
-      if (l > 0.f) {
-        const float w = l * __expf(pr[D] - gmax);
-        num = fmaf(w, pr[d], num);
+      const float ov = fetch(g, d);
+      if (gl[g] > 0.f) {
+        const float w = gl[g] * __expf(gm[g] - gmax);
+        num = fmaf(w, ov, num);
         den += w;
       }
     }
     if (a.out) reinterpret_cast<T*>(a.out)[b * a.o_stride[0] + hq * a.o_stride[1] + d] = from_f<T>(den > 0.f ? num / den : 0.f);
   }
+  if (timed_out) set_err(a.err, TASFT_DEVERR_TIMEOUT);
   // the last row's CTA to finish advances the epoch (every CTA read it on entry)
   __syncthreads();
   if (threadIdx.x == 0) {

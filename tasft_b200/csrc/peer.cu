@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_combine_kernel(tasft_peer_c
   const int64_t slab = rows * (D + 2);  // floats of one rank's partial
   const uint32_t e = *a.epoch + 1u;
   const int par = (int)(e & 1u);
-  const int64_t foff = peer_part_off(world, rows);  // float offset of the partials
+  const int64_t foff = peer_part_off(world, rows, D);  // float offset of the partials
   // 1. push this rank's (o | m, l) rows into slot [par][rank] of every mailbox, 8 bytes per
   //    store (a row is D + 2 floats, D even: rows stay 8-byte aligned)
   const int64_t rp = (D + 2) / 2;  // float2 per mailbox row

@@ -32,19 +32,29 @@ def _mailbox(world, rows, D):
     return torch.zeros(nbytes // 4, dtype=torch.int32, device=DEV)
 
 
-def _part_off(world, rows):
-    """Float offset of the partials in a mailbox: call flags (world + 1 words) and row flags
-    (world x rows words), each padded to 256 bytes."""
-    return (((world + 1) * 4 + 255) // 256 * 256 + (world * rows * 4 + 255) // 256 * 256) // 4
+def _flags_bytes(world):
+    return ((world + 1) * 4 + 255) // 256 * 256
 
 
-def _rowflags(box, world, rows):
-    base = ((world + 1) * 4 + 255) // 256 * 256 // 4
-    return box[base: base + world * rows].view(world, rows)
+def _part_off(world, rows, D):
+    """Float offset of the partials in a mailbox: call flags (world + 1 words, padded to 256
+    bytes), then the row words (2 x world x rows x (D + 2) 8-byte words)."""
+    return (_flags_bytes(world) + 2 * world * rows * (D + 2) * 8) // 4
+
+
+def _words(box, world, rows, D, par, r):
+    """Slot [par][r] of the row words, [rows, D + 2] int64 (fp32 bits | epoch << 32)."""
+    base = _flags_bytes(world) // 8 + (par * world + r) * rows * (D + 2)
+    return box.view(torch.int64)[base: base + rows * (D + 2)].view(rows, D + 2)
+
+
+def _pack(values, epoch):
+    bits = values.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    return bits | (epoch << 32)
 
 
 def _slot(box, world, rows, D, par, r):
-    foff = _part_off(world, rows)
+    foff = _part_off(world, rows, D)
     slab = rows * (D + 2)
     return box.view(torch.float32)[foff + (par * world + r) * slab: foff + (par * world + r + 1) * slab].view(rows, D + 2)
 
@@ -129,7 +139,8 @@ def test_fused_decode_exchange_emulated_twice():
     """Rank 0 of 2 on one GPU: rank 1's rows (its own slab decoded with partials) and row
     flags are written into rank 0's mailbox by the host; the fused call must agree with the
     NCCL path's combine of the two slabs' partials and with a one-rank decode of the whole
-    cache, leave its own rows and flags in rank 1's mailbox, and advance the epoch."""
+    cache, leave its own rows (tagged with the epoch) in rank 1's mailbox, and advance the
+    epoch."""
     q, kc, vc, kv_len, kept, nb = _slab_case()
     B, Hq, D = q.shape
     rows, world, half = B * Hq, 2, nb // 2
@@ -148,8 +159,7 @@ def test_fused_decode_exchange_emulated_twice():
     full = T.bsa_decode(q, kc, vc, kv_len, kept, 64)
     for call in (1, 2):
         par = call & 1
-        _slot(boxes[0], world, rows, D, par, 1).copy_(torch.cat([parts[1][0], parts[1][1]], -1))
-        _rowflags(boxes[0], world, rows)[1].fill_(call)
+        _words(boxes[0], world, rows, D, par, 1).copy_(_pack(torch.cat([parts[1][0], parts[1][1]], -1), call))
         out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=DEV)
         T.decode.bsa_decode_peer(q, slabs[0][0], slabs[0][1], kv_len, parts[0][2], peer, 64, workspace=ws, out=out)
         torch.cuda.synchronize()
@@ -160,17 +170,18 @@ def test_fused_decode_exchange_emulated_twice():
         # in-kernel merge (16 splits): same maths, fp32 summation orders differ
         assert (out.float() - ref.float()).abs().max().item() <= 1e-2
         assert (out.float() - full.float()).abs().max().item() <= 2e-2
-        pushed = _slot(boxes[1], world, rows, D, par, 0)
+        pushed = _words(boxes[1], world, rows, D, par, 0)
+        assert bool(((pushed >> 32) == call).all())  # every word carries this call's epoch
+        vals = (pushed & 0xFFFFFFFF).to(torch.int32).view(torch.float32)
         own = torch.cat([parts[0][0], parts[0][1]], -1)
-        assert torch.allclose(pushed, own, rtol=1e-4, atol=1e-5)
-        assert bool((_rowflags(boxes[1], world, rows)[0] == call).all())
+        assert torch.allclose(vals, own, rtol=1e-4, atol=1e-5)
 
 
 def test_fused_decode_exchange_missing_peer_times_out():
     q, kc, vc, kv_len, kept, nb = _slab_case()
     B, Hq, D = q.shape
     boxes = [_mailbox(2, B * Hq, D), _mailbox(2, B * Hq, D)]
-    peer = _Peer(boxes, 0, int(5e7))  # rank 1's row flags are never raised
+    peer = _Peer(boxes, 0, int(5e7))  # rank 1's words never arrive
     ws = T.DecodeWorkspace(B, Hq, 4, D, 64, DEV)
     half = nb // 2
     out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=DEV)
