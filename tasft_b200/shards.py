@@ -183,11 +183,13 @@ def long_context_decode(
 
 
 class PeerExchange:
-    """Merge of split-KV decode partials across the ranks of ``group`` over peer memory
-    (``tasft_peer_combine``): each rank pushes its partial into every rank's mailbox through
-    CUDA IPC mappings and merges what its own mailbox holds. No NCCL call per step, so the
-    step can be captured in a CUDA graph. Set up once (collective: every rank constructs it
-    in the same order); ``close()`` unmaps and frees."""
+    """Mailboxes for exchanging split-KV decode partials across the ranks of ``group`` over
+    peer memory: every rank's mailbox is mapped into every other rank through CUDA IPC.
+    ``bsa_decode_peer`` uses them from inside the decode's merge kernel (each rank stores its
+    rows into every mailbox and merges what its own holds); calling the object runs the
+    stand-alone merge kernel (``tasft_peer_combine``) on given partials. No NCCL call per
+    step, so the step can be captured in a CUDA graph. Set up once (collective: every rank
+    constructs it in the same order); ``close()`` unmaps and frees."""
 
     def __init__(self, rows: int, D: int, device, group=None, timeout_s: float = 1.0) -> None:
         import ctypes as C  # noqa: PLC0415
