@@ -455,7 +455,8 @@ def bench_qwen_prefill(rank, ws, dev, flush, args, peaks):
                       "sparsity (kv-head masks from the random-init gate)",
             "gflop": round(flops / 1e9, 2), "ms": round(ms_max, 4),
             "tflops": round(flops / (ms_max * 1e-3) / 1e12, 2),
-            "frac": round(flops / (ms_max * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+            # of the measured peak of all the ranks' GPUs together
+            "frac": round(flops / (ms_max * 1e-3) / 1e12 / (peaks["bf16_tflops"] * ws), 4),
             "split": f"q-block ranges of equal kept work over {ws} rank(s)" if ws > 1 else "one GPU",
             "scaling": "strong"}
     if ws > 1:
