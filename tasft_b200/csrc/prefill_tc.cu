@@ -289,10 +289,13 @@ __global__ void __launch_bounds__(kThreads, 2)
           ok = false;
         }
         if (ok) {
-          const int nvalid = (w.valid[0] ? 1 : 0) + (w.valid[1] ? 1 : 0);
+          // a tile that keeps nothing (e.g. q-blocks outside this rank's range) needs no Q:
+          // its phase completes on the arrival alone
+          const bool need_q = w.n > 0;
+          const int nvalid = need_q ? (w.valid[0] ? 1 : 0) + (w.valid[1] ? 1 : 0) : 0;
           mbar_arrive_expect_tx(q_full, nvalid * L::kChunks * 64 * 128);
           for (int s = 0; s < 2; ++s) {
-            if (!w.valid[s]) continue;
+            if (!w.valid[s] || !need_q) continue;
             for (int c = 0; c < L::kChunks; ++c)
               tc::tma_load_4d(sQ + c * 128 * 128 + s * 64 * 128, &tmq, c * 64, w.row0 + w.qbs[s] * kBlk, w.head[s],
                               cu ? 0 : w.b,
