@@ -264,21 +264,35 @@ __global__ void loss_add_kernel(float* d, int64_t n, const float* gsp) {
 // Gate backward: soft = sigmoid(w_out . relu(a_i + c_j)) (zeroed above the diagonal)
 // ---------------------------------------------------------------------------
 // A [rows_q, hid] = W_q pq + b ; Ct [B*Hk, hid, NBk] = W_k pk
+// A = W_q pq + b, Ct = W_k pk (transposed) recomputed from the block means: one warp per
+// row, lanes over d (coalesced reads of the means row and of each W_in row, which stays in
+// L1), a warp sum per hidden unit.
 __global__ void bwd_project_kernel(tasft_gate_bwd_args a, float* A, float* Ct) {
-  const int64_t rq = (int64_t)a.B * a.Hq * a.NBq;
-  int64_t r = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rq = (int64_t)a.B * a.Hq * a.NBq, rk = (int64_t)a.B * a.Hk * a.NBk;
+  int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (r >= rq + rk) return;
   const bool isq = r < rq;
   if (!isq) r -= rq;
   const float* x = (isq ? a.pooled_q : a.pooled_k) + r * a.D;
   const int off = isq ? 0 : a.D;
-  for (int h = threadIdx.x; h < a.hidden; h += blockDim.x) {
+  float xv[8];  // D <= 256: lane holds x[lane + 32 k]
+#pragma unroll
+  for (int k = 0; k < 8; ++k) xv[k] = lane + 32 * k < a.D ? x[lane + 32 * k] : 0.f;
+  for (int h = 0; h < a.hidden; ++h) {
     const float* w = a.w_in + (int64_t)h * 2 * a.D + off;
     float s = 0.f;
-    for (int d = 0; d < a.D; ++d) s = fmaf(w[d], x[d], s);
-    if (isq) A[r * a.hidden + h] = s + a.b_in[h];
-    else {
-      const int64_t bh = r / a.NBk, j = r % a.NBk;
-      Ct[(bh * a.hidden + h) * a.NBk + j] = s;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (lane + 32 * k < a.D) s = fmaf(__ldg(w + lane + 32 * k), xv[k], s);
+    s = warp_sum(s);
+    if (lane == 0) {
+      if (isq) {
+        A[r * a.hidden + h] = s + a.b_in[h];
+      } else {
+        const int64_t bh = r / a.NBk, j = r % a.NBk;
+        Ct[(bh * a.hidden + h) * a.NBk + j] = s;
+      }
     }
   }
 }
@@ -297,12 +311,16 @@ __global__ void bwd_rows_kernel(tasft_gate_bwd_args a, const float* A, const flo
   const int hq = (int)((row / a.NBq) % a.Hq), b = (int)(row / ((int64_t)a.NBq * a.Hq));
   const int hk = hq / (a.Hq / a.Hk);
   const float* ct = Ct + ((int64_t)b * a.Hk + hk) * a.hidden * a.NBk;
+  // this lane's d logit for its first k-blocks (the rest recomputed when NBk > 256)
+  float dlv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) dlv[k] = lane + 32 * k < a.NBk ? dlogit_of(a, row * a.NBk + lane + 32 * k) : 0.f;
   for (int h = 0; h < a.hidden; ++h) {
     const float ai = A[row * a.hidden + h];
     const float wh = a.w_out[h];
     float da = 0.f, dw = 0.f;
-    for (int j = lane; j < a.NBk; j += 32) {
-      const float dl = dlogit_of(a, row * a.NBk + j);
+    for (int j = lane, k = 0; j < a.NBk; j += 32, ++k) {
+      const float dl = k < 8 ? dlv[k & 7] : dlogit_of(a, row * a.NBk + j);
       const float pre = ai + ct[(int64_t)h * a.NBk + j];
       if (pre > 0.f) {
         da = fmaf(dl, wh, da);
@@ -318,7 +336,10 @@ __global__ void bwd_rows_kernel(tasft_gate_bwd_args a, const float* A, const flo
   }
 }
 
-// cols: one warp per (b, hk, j); dC[col][h] summed over the group's q-heads and rows
+// cols: one warp per (b, hk, j); dC[col][h] summed over the group's q-heads and rows.
+// Lanes take rows; a lane computes its row's d logit once and runs over the hidden units
+// with its row of A (contiguous) against c_j (in registers); per-unit warp sums at the end.
+template <int HID>
 __global__ void bwd_cols_kernel(tasft_gate_bwd_args a, const float* A, const float* Ct, float* dC) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t col = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
@@ -329,14 +350,55 @@ __global__ void bwd_cols_kernel(tasft_gate_bwd_args a, const float* A, const flo
   const int hk = (int)(bhk % a.Hk), b = (int)(bhk / a.Hk);
   const int grp = a.Hq / a.Hk;
   const int rows = grp * a.NBq;
+  float cj[HID], wo[HID], dc[HID];
+#pragma unroll
+  for (int h = 0; h < HID; ++h) {
+    cj[h] = Ct[(bhk * HID + h) * a.NBk + j];
+    wo[h] = a.w_out[h];
+    dc[h] = 0.f;
+  }
+  for (int t = lane; t < rows; t += 32) {
+    const int g = t / a.NBq, i = t % a.NBq;
+    const int64_t row = ((int64_t)b * a.Hq + hk * grp + g) * a.NBq + i;
+    const float dl = dlogit_of(a, row * a.NBk + j);
+    const float4* ar = reinterpret_cast<const float4*>(A + row * HID);
+#pragma unroll
+    for (int h4 = 0; h4 < HID / 4; ++h4) {
+      const float4 av = ar[h4];
+      const float pv[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = 4 * h4 + e;
+        if (pv[e] + cj[h] > 0.f) dc[h] = fmaf(dl, wo[h], dc[h]);
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HID; ++h) {
+    const float v = warp_sum(dc[h]);
+    if (lane == 0) dC[col * HID + h] = v;
+  }
+}
+
+// Any hidden width: one unit at a time.
+__global__ void bwd_cols_any_kernel(tasft_gate_bwd_args a, const float* A, const float* Ct, float* dC) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t col = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  const int64_t cols = (int64_t)a.B * a.Hk * a.NBk;
+  if (col >= cols) return;
+  const int j = (int)(col % a.NBk);
+  const int64_t bhk = col / a.NBk;
+  const int hk = (int)(bhk % a.Hk), b = (int)(bhk / a.Hk);
+  const int grp = a.Hq / a.Hk;
+  const int rows = grp * a.NBq;
   for (int h = 0; h < a.hidden; ++h) {
-    const float cj = Ct[(bhk * a.hidden + h) * a.NBk + j];
+    const float cjh = Ct[(bhk * a.hidden + h) * a.NBk + j];
     const float wh = a.w_out[h];
     float dc = 0.f;
     for (int t = lane; t < rows; t += 32) {
       const int g = t / a.NBq, i = t % a.NBq;
       const int64_t row = ((int64_t)b * a.Hq + hk * grp + g) * a.NBq + i;
-      const float pre = A[row * a.hidden + h] + cj;
+      const float pre = A[row * a.hidden + h] + cjh;
       if (pre > 0.f) dc = fmaf(dlogit_of(a, row * a.NBk + j), wh, dc);
     }
     dc = warp_sum(dc);
@@ -631,9 +693,14 @@ extern "C" int tasft_gate_bwd(const tasft_gate_bwd_args* ap, tasft_stream_t stre
   float* Ct = dwo + rq * a.hidden;
   float* dC = Ct + rk * a.hidden;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  bwd_project_kernel<<<(unsigned)(rq + rk), 64, 0, st>>>(a, A, Ct);
+  bwd_project_kernel<<<(unsigned)ceil_div(rq + rk, 8), 256, 0, st>>>(a, A, Ct);
   bwd_rows_kernel<<<ceil_div(rq, 8), 256, 0, st>>>(a, A, Ct, dA, dwo);
-  bwd_cols_kernel<<<ceil_div(rk, 8), 256, 0, st>>>(a, A, Ct, dC);
+  if (a.hidden == 32)
+    bwd_cols_kernel<32><<<ceil_div(rk, 8), 256, 0, st>>>(a, A, Ct, dC);
+  else if (a.hidden == 64)
+    bwd_cols_kernel<64><<<ceil_div(rk, 8), 256, 0, st>>>(a, A, Ct, dC);
+  else
+    bwd_cols_any_kernel<<<ceil_div(rk, 8), 256, 0, st>>>(a, A, Ct, dC);
   const int cq = (int)ceil_div(rq, kWChunk), ck = (int)ceil_div(rk, kWChunk);
   float* part = dC + rk * a.hidden;
   float* part_b = part + (int64_t)(cq + ck) * a.hidden * a.D;
