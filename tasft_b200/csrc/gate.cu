@@ -297,6 +297,135 @@ __global__ void __launch_bounds__(kPoolThreads, 3) gate_pool_project_fused_kerne
   }
 }
 
+// Persistent form of the fused kernel for bf16 (one warp per block as above): each warp
+// walks blocks with a stride of the grid's warps and, before projecting a block, puts the
+// first 8 row loads of its next block in flight, so the warp's reads do not stop while it
+// computes the projection.
+template <int CV, int HID, int RS>
+__global__ void __launch_bounds__(kPoolThreads, 2) gate_pool_project_stream_kernel(tasft_gate_args a, float* A,
+                                                                                  float* Ct, int NBq, int NBk) {
+  constexpr int EPV = 8;
+  constexpr int D = EPV * CV;
+  constexpr int HR = HID / RS;
+  constexpr int NOUT = HR / CV;
+  constexpr int kPre = 8;  // rows per lane put in flight ahead
+  static_assert(HR % CV == 0 && CV * RS == 32, "one warp per block");
+  using T = __nv_bfloat16;
+  const int lane = threadIdx.x & 31;
+  const int c = lane % CV, rs = lane / CV;
+  const int64_t nq = (int64_t)a.B * a.Hq * NBq, nk = (int64_t)a.B * a.Hk * NBk, total = nq + nk;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  struct Blk {
+    const T* p;  // this lane's first row (row rs, column c)
+    int64_t rstr;
+    int rows;
+  };
+  auto locate = [&](int64_t it) -> Blk {
+    const bool isq = it < nq;
+    const int64_t r = isq ? it : it - nq;
+    const int H = isq ? a.Hq : a.Hk, NB = isq ? NBq : NBk, S = isq ? a.Sq : a.Sk;
+    const int blk = (int)(r % NB);
+    const int64_t bh = r / NB;
+    const int h = (int)(bh % H), b = (int)(bh / H);
+    const int64_t* st = isq ? a.q_stride : a.k_stride;
+    Blk k;
+    k.rstr = st[2];
+    k.p = reinterpret_cast<const T*>(isq ? a.q : a.k) + b * st[0] + h * st[1] + ((int64_t)blk * a.block + rs) * k.rstr +
+          c * EPV;
+    k.rows = min(a.block, S - blk * a.block);
+    return k;
+  };
+  uint4 pre[kPre];
+  auto prefetch = [&](const Blk& k) {
+#pragma unroll
+    for (int i = 0; i < kPre; ++i)
+      pre[i] = rs + RS * i < k.rows ? __ldg(reinterpret_cast<const uint4*>(k.p + (int64_t)RS * i * k.rstr))
+                                    : make_uint4(0u, 0u, 0u, 0u);
+  };
+  Blk cur{};
+  if (item < total) {
+    cur = locate(item);
+    prefetch(cur);
+  }
+  for (; item < total; item += nw) {
+    uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) add_bf16x8(pre[i], acc);
+    {
+      const T* p = cur.p + (int64_t)RS * kPre * cur.rstr;
+#pragma unroll 8
+      for (int r = rs + RS * kPre; r < cur.rows; r += RS, p += RS * cur.rstr)
+        add_bf16x8(__ldg(reinterpret_cast<const uint4*>(p)), acc);
+    }
+    // the next block's first rows go out now, ahead of this block's projection
+    const int64_t nxt = item + nw;
+    Blk nb{};
+    if (nxt < total) {
+      nb = locate(nxt);
+      prefetch(nb);
+    }
+    float f[EPV];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float((uint32_t)acc[i]);
+      f[2 * i + 1] = __uint_as_float((uint32_t)(acc[i] >> 32));
+    }
+#pragma unroll
+    for (int e = 0; e < EPV; ++e)
+#pragma unroll
+      for (int d = CV; d < 32; d <<= 1) f[e] += __shfl_xor_sync(0xffffffffu, f[e], d);
+    const float inv = 1.0f / (float)a.block;
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) f[e] *= inv;
+    const bool isq = item < nq;
+    const int64_t row = isq ? item : item - nq;  // (b * H + h) * NB + blk
+    float* pooled = isq ? a.pooled_q : a.pooled_k;
+    if (pooled && rs == 0) {
+      float* out = pooled + row * D + c * EPV;
+#pragma unroll
+      for (int e = 0; e < EPV; e += 4) *reinterpret_cast<float4*>(out + e) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
+    }
+    float v[HR];
+    const float* w = a.w_in + (int64_t)rs * HR * 2 * D + (isq ? 0 : D) + c * EPV;
+#pragma unroll
+    for (int j = 0; j < HR; ++j) {
+      float sacc = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPV; e += 4) {
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w + (int64_t)j * 2 * D + e));
+        sacc = fmaf(wv.x, f[e], fmaf(wv.y, f[e + 1], fmaf(wv.z, f[e + 2], fmaf(wv.w, f[e + 3], sacc))));
+      }
+      v[j] = sacc;
+    }
+    int n = HR;
+#pragma unroll
+    for (int d = CV / 2; d >= 1; d >>= 1) {
+      const bool upper = (c & d) != 0;
+      n >>= 1;
+#pragma unroll
+      for (int i = 0; i < HR / 2; ++i) {
+        if (i < n) {
+          const float send = upper ? v[i] : v[i + n];
+          const float keep = upper ? v[i + n] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+      }
+    }
+    const int j0 = rs * HR + c * NOUT;
+    if (isq) {
+#pragma unroll
+      for (int i = 0; i < NOUT; ++i) A[row * HID + j0 + i] = v[i] + a.b_in[j0 + i];
+    } else {
+      const int64_t bh = row / NBk, blk = row % NBk;
+#pragma unroll
+      for (int i = 0; i < NOUT; ++i) Ct[(bh * HID + j0 + i) * NBk + blk] = v[i];
+    }
+    cur = nb;
+  }
+  pdl_trigger();
+}
+
 template <int HID>
 __global__ void __launch_bounds__(kPoolThreads) gate_project_kernel(tasft_gate_args a, const float* mq,
                                                                    const float* mk, float* A, float* Ct, int NBq,
@@ -616,7 +745,23 @@ static int launch_pool(const tasft_gate_args& a, float* A, float* Ct, float* mq,
                          aligned16(a.w_in);
   // row groups per block in the fused kernel: a block takes a whole warp (CV * RS = 32)
   const int RS = 32 / (CV > 0 ? CV : 1);
-  if (vec_ok && EPV == 8 && (a.D == 64 || a.D == 128) && (a.hidden == 32 || a.hidden == 64) && pooled_ok &&
+  if (std::is_same<T, __nv_bfloat16>::value && vec_ok && (a.D == 64 || a.D == 128) &&
+      (a.hidden == 32 || a.hidden == 64) && pooled_ok && !std::getenv("TASFT_GATE_UNFUSED")) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t items = (int64_t)a.B * a.Hq * NBq + (int64_t)a.B * a.Hk * NBk;
+    int64_t blocks = (int64_t)sms * 2;
+    if (blocks * (kPoolThreads / 32) > items) blocks = ceil_div(items, kPoolThreads / 32);
+    auto go = [&](auto kern) { kern<<<(unsigned)blocks, kPoolThreads, 0, st>>>(a, A, Ct, NBq, NBk); };
+    if (a.D == 128) {
+      if (a.hidden == 32) go(gate_pool_project_stream_kernel<16, 32, 2>);
+      else go(gate_pool_project_stream_kernel<16, 64, 2>);
+    } else {
+      if (a.hidden == 32) go(gate_pool_project_stream_kernel<8, 32, 4>);
+      else go(gate_pool_project_stream_kernel<8, 64, 4>);
+    }
+  } else   if (vec_ok && EPV == 8 && (a.D == 64 || a.D == 128) && (a.hidden == 32 || a.hidden == 64) && pooled_ok &&
       nthreads * RS < (1LL << 31) - kPoolThreads && !std::getenv("TASFT_GATE_UNFUSED")) {
     const unsigned blocks = (unsigned)ceil_div(nthreads * RS, kPoolThreads);
     auto go = [&](auto kern) { kern<<<blocks, kPoolThreads, 0, st>>>(a, A, Ct, NBq, NBk); };
