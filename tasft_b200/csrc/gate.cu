@@ -128,6 +128,10 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 //     row-major; thread (row octet, hidden unit) accumulates 8 outputs, reading its weight
 //     once per d and the means as warp-wide broadcasts.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
+  return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+
 __device__ __forceinline__ void add_bf16x8(const uint4& u, uint64_t (&acc)[4]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -595,8 +599,18 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_slab_kernel(tasft_
   // launched early (programmatic dependent launch) behind the pooling kernel: wait for its
   // results; a no-op when launched normally
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if constexpr (HID > 0) {
+    // [unit pair][k-block][2]: a lane's two units of one k-block are one 8-byte word, and the
+    // lanes of a warp (consecutive k-blocks) read consecutive words
 #pragma unroll 8
-  for (int x = threadIdx.x; x < hid * NBk; x += blockDim.x) ct[x] = __ldg(src + x);
+    for (int x = threadIdx.x; x < hid * NBk; x += blockDim.x) {
+      const int h = x / NBk, j = x % NBk;
+      ct[((h >> 1) * NBk + j) * 2 + (h & 1)] = __ldg(src + x);
+    }
+  } else {
+#pragma unroll 8
+    for (int x = threadIdx.x; x < hid * NBk; x += blockDim.x) ct[x] = __ldg(src + x);
+  }
   for (int x = threadIdx.x; x < nrows * hid; x += blockDim.x) {
     const int r = x / hid, lr = lr0 + r;
     const int64_t row = ((int64_t)b * a.Hq + hk * grp + lr / NBq) * NBq + lr % NBq;
@@ -618,15 +632,17 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_slab_kernel(tasft_
     const int64_t row = ((int64_t)b * a.Hq + hk * grp + lr / NBq) * NBq + i;
     const float* ar = arows + r * hid;
     int cnt = 0, kept_total = 0;
-    float arr[HID > 0 ? HID : 1];  // this row's a_i, and w_out, in registers (HID known)
-    float wr[HID > 0 ? HID : 1];
+    uint64_t arr2[HID > 0 ? HID / 2 : 1];  // this row's a_i, and w_out, in registers (HID known),
+    uint64_t wr2[HID > 0 ? HID / 2 : 1];   // as (unit h, unit h + 1) pairs
     if constexpr (HID > 0) {
 #pragma unroll
       for (int h = 0; h < HID; h += 4) {
         const float4 av = *reinterpret_cast<const float4*>(ar + h);
         const float4 wv = *reinterpret_cast<const float4*>(wout + h);
-        arr[h] = av.x; arr[h + 1] = av.y; arr[h + 2] = av.z; arr[h + 3] = av.w;
-        wr[h] = wv.x; wr[h + 1] = wv.y; wr[h + 2] = wv.z; wr[h + 3] = wv.w;
+        arr2[h >> 1] = pack_f2(av.x, av.y);
+        arr2[(h >> 1) + 1] = pack_f2(av.z, av.w);
+        wr2[h >> 1] = pack_f2(wv.x, wv.y);
+        wr2[(h >> 1) + 1] = pack_f2(wv.z, wv.w);
       }
     }
     for (int j0 = 0; j0 < NBk; j0 += 32) {
@@ -636,11 +652,21 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) gate_pair_slab_kernel(tasft_
       if (in_range) {
         float l0 = 0.f, l1 = 0.f;
         if constexpr (HID > 0) {
+          // units h (even chain) and h + 1 (odd chain) side by side in packed f32x2 ops: the same
+          // per-lane roundings as two scalar chains
+          uint64_t acc = 0;
+          const float2* c2 = reinterpret_cast<const float2*>(ct) + j;
 #pragma unroll
           for (int h = 0; h < HID; h += 2) {
-            l0 = fmaf(wr[h], fmaxf(arr[h] + ct[h * NBk + j], 0.f), l0);
-            l1 = fmaf(wr[h + 1], fmaxf(arr[h + 1] + ct[(h + 1) * NBk + j], 0.f), l1);
+            const float2 cv = c2[(h >> 1) * NBk];
+            uint64_t pre;
+            asm("add.f32x2 %0, %1, %2;" : "=l"(pre) : "l"(arr2[h >> 1]), "l"(pack_f2(cv.x, cv.y)));
+            const uint64_t rl = pack_f2(fmaxf(__uint_as_float((uint32_t)pre), 0.f),
+                                        fmaxf(__uint_as_float((uint32_t)(pre >> 32)), 0.f));
+            asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(wr2[h >> 1]), "l"(rl));
           }
+          l0 = __uint_as_float((uint32_t)acc);
+          l1 = __uint_as_float((uint32_t)(acc >> 32));
         } else {
           int h = 0;
           for (; h + 1 < hid; h += 2) {
