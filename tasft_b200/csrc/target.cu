@@ -336,6 +336,64 @@ __global__ void bwd_rows_kernel(tasft_gate_bwd_args a, const float* A, const flo
   }
 }
 
+// rows, hidden 32 / 64: lanes take k-blocks and keep per-unit sums in registers over all of
+// them (the d logit of a (row, k-block) computed once); a butterfly reduce-scatter over the
+// warp then leaves unit h's totals in lane h % 32 (HID / 32 units per lane), so the row
+// costs about 2 HID shuffles instead of 10 per unit.
+template <int HID>
+__global__ void bwd_rows_rs_kernel(tasft_gate_bwd_args a, const float* A, const float* Ct, float* dA, float* dwo) {
+  constexpr int U = HID / 32;  // units per lane after the reduction
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  const int64_t rows = (int64_t)a.B * a.Hq * a.NBq;
+  if (row >= rows) return;
+  const int hq = (int)((row / a.NBq) % a.Hq), b = (int)(row / ((int64_t)a.NBq * a.Hq));
+  const int hk = hq / (a.Hq / a.Hk);
+  const float* ct = Ct + ((int64_t)b * a.Hk + hk) * HID * a.NBk;
+  float ai[HID], da[HID], dw[HID];
+#pragma unroll
+  for (int h = 0; h < HID; ++h) {
+    ai[h] = A[row * HID + h];
+    da[h] = 0.f;
+    dw[h] = 0.f;
+  }
+  for (int j = lane; j < a.NBk; j += 32) {
+    const float dl = dlogit_of(a, row * a.NBk + j);
+#pragma unroll
+    for (int h = 0; h < HID; ++h) {
+      const float pre = ai[h] + ct[(int64_t)h * a.NBk + j];
+      if (pre > 0.f) {
+        da[h] += dl;  // times w_out[h] after the reduction
+        dw[h] = fmaf(dl, pre, dw[h]);
+      }
+    }
+  }
+  // reduce-scatter: after the step with offset d, lane l keeps the half of the units whose
+  // bit d matches its own
+  int n = HID;
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) {
+    const bool upper = (lane & d) != 0;
+    n >>= 1;
+#pragma unroll
+    for (int i = 0; i < HID / 2; ++i) {
+      if (i < n) {
+        const float sa = upper ? da[i] : da[i + n], ka = upper ? da[i + n] : da[i];
+        const float sw = upper ? dw[i] : dw[i + n], kw = upper ? dw[i + n] : dw[i];
+        da[i] = ka + __shfl_xor_sync(0xffffffffu, sa, d);
+        dw[i] = kw + __shfl_xor_sync(0xffffffffu, sw, d);
+      }
+    }
+  }
+  // lane l now holds units l * U .. l * U + U - 1
+#pragma unroll
+  for (int i = 0; i < U; ++i) {
+    const int h = lane * U + i;
+    dA[row * HID + h] = da[i] * a.w_out[h];
+    dwo[row * HID + h] = dw[i];
+  }
+}
+
 // cols: one warp per (b, hk, j); dC[col][h] summed over the group's q-heads and rows.
 // Lanes take rows; a lane computes its row's d logit once and runs over the hidden units
 // with its row of A (contiguous) against c_j (in registers); per-unit warp sums at the end.
@@ -694,7 +752,12 @@ extern "C" int tasft_gate_bwd(const tasft_gate_bwd_args* ap, tasft_stream_t stre
   float* dC = Ct + rk * a.hidden;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   bwd_project_kernel<<<(unsigned)ceil_div(rq + rk, 8), 256, 0, st>>>(a, A, Ct);
-  bwd_rows_kernel<<<ceil_div(rq, 8), 256, 0, st>>>(a, A, Ct, dA, dwo);
+  if (a.hidden == 32)
+    bwd_rows_rs_kernel<32><<<ceil_div(rq, 8), 256, 0, st>>>(a, A, Ct, dA, dwo);
+  else if (a.hidden == 64)
+    bwd_rows_rs_kernel<64><<<ceil_div(rq, 8), 256, 0, st>>>(a, A, Ct, dA, dwo);
+  else
+    bwd_rows_kernel<<<ceil_div(rq, 8), 256, 0, st>>>(a, A, Ct, dA, dwo);
   if (a.hidden == 32)
     bwd_cols_kernel<32><<<ceil_div(rk, 8), 256, 0, st>>>(a, A, Ct, dC);
   else if (a.hidden == 64)
