@@ -446,7 +446,8 @@ def bench_qwen_prefill(rank, ws, dev, flush, args, peaks):
     my_blocks = int(mine.cnt.sum().item())
     kern = T.BlockSparseFlashAttention(block_size=c["block"])
     out = torch.empty_like(q)
-    t = time_steps(lambda: kern.forward(q, k, v, mine, out=out), args.steps, args.warmup, flush, ws)
+    rng = (lo, hi) if ws > 1 else None  # the rank visits only its q-block window
+    t = time_steps(lambda: kern.forward(q, k, v, mine, out=out, q_block_range=rng), args.steps, args.warmup, flush, ws)
     ms = statistics.mean(t)
     ms_max = max_over_ranks(ms, ws)
     unit = grp * 4 * c["block"] * c["block"] * c["D"]

@@ -56,7 +56,7 @@
 extern "C" {
 #endif
 
-#define TASFT_ABI_VERSION 2
+#define TASFT_ABI_VERSION 3
 
 /* status codes (host-side, returned) */
 #define TASFT_OK                  0
@@ -201,6 +201,10 @@ typedef struct {
   int32_t Hm;             /* heads of the lists: Hq (per q-head) or Hk (per kv-head) */
   int32_t* err;           /* optional device error word */
   int32_t force_simt;     /* 1 = use the CUDA-core kernel even where tcgen05 applies (testing) */
+  int32_t qb_lo, qb_hi;   /* q-block window [qb_lo, qb_hi) (one rank's share of a long sequence);
+                             qb_hi <= 0: every q-block. The tcgen05 kernel visits only the window's
+                             tiles and leaves the other output rows untouched (the CUDA-core kernel
+                             computes every row); padded layout only */
 } tasft_prefill_args;
 TASFT_API int tasft_bsa_prefill_fwd(const tasft_prefill_args* args, tasft_stream_t stream);
 

@@ -78,7 +78,8 @@ class PrefillArgs(C.Structure):
         ("q_stride", I64x4), ("k_stride", I64x4), ("v_stride", I64x4), ("o_stride", I64x4),
         ("B", C.c_int32), ("Hq", C.c_int32), ("Hk", C.c_int32), ("S", C.c_int32), ("D", C.c_int32),
         ("block", C.c_int32), ("dtype", C.c_int32), ("causal", C.c_int32), ("scale", C.c_float),
-        ("kept_idx", vp), ("kept_cnt", vp), ("Hm", C.c_int32), ("err", vp), ("force_simt", C.c_int32),
+        ("kept_idx", vp), ("kept_cnt", vp), ("Hm", C.c_int32), ("err", vp), ("force_simt", C.c_int32), ("qb_lo", C.c_int32),
+        ("qb_hi", C.c_int32),
     ]
 
 

@@ -153,8 +153,14 @@ class BlockSparseFlashAttention:
         causal: bool = True,
         out: torch.Tensor | None = None,
         err: torch.Tensor | None = None,
+        q_block_range: tuple[int, int] | None = None,
     ) -> torch.Tensor:
-        """Block-sparse attention; returns a new ``[B, Hq, S, D]`` tensor in q's dtype."""
+        """Block-sparse attention; returns a new ``[B, Hq, S, D]`` tensor in q's dtype.
+
+        ``q_block_range=(lo, hi)``: compute only the rows of q-blocks ``[lo, hi)`` (one rank's
+        share of a long sequence, ``shards.qblock_ranges``); the tensor-core kernel then visits
+        only those tiles and leaves the other rows of ``out`` as they were (the CUDA-core
+        kernel computes every row)."""
         self._validate_inputs(q, k, v, block_mask)
         B, Hq, S, D = q.shape
         Hk = k.shape[1]
@@ -175,6 +181,7 @@ class BlockSparseFlashAttention:
             B=B, Hq=Hq, Hk=Hk, S=S, D=D, block=self.block_size, dtype=L.dtype_code(q), causal=int(causal),
             scale=1.0 / math.sqrt(D), kept_idx=idx.data_ptr(), kept_cnt=cnt.data_ptr(), Hm=idx.shape[1],
             err=L.ptr(err), force_simt=int(self.force_simt),
+            qb_lo=int(q_block_range[0]) if q_block_range else 0, qb_hi=int(q_block_range[1]) if q_block_range else 0,
         )
         L.check(L.lib().tasft_bsa_prefill_fwd(args, L.stream_ptr(q.device)), "tasft_bsa_prefill_fwd",
                 shape=[B, Hq, Hk, S, D], block=self.block_size)

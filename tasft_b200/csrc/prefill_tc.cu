@@ -102,12 +102,15 @@ struct Smem {
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
-// Tile id -> work. Ids run heavy (late) q-blocks first. With `cu` (packed sequences of
-// different lengths) q-blocks past a sequence's end are marked invalid.
-__device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, const int32_t* cu, int NB, int id) {
+// Tile id -> work. Ids run heavy (late) q-blocks first, over the q-block window [qlo, qhi)
+// (all q-blocks unless the caller restricts it). With `cu` (packed sequences of different
+// lengths) q-blocks past a sequence's end are marked invalid.
+__device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, const int32_t* cu, int NB, int id, int qlo,
+                                            int qhi) {
   const int grp = a.Hq / a.Hk;
   const int pairs = grp >= 2 ? (grp + 1) / 2 : 1;
-  const int nbp = grp >= 2 ? NB : (NB + 1) / 2;
+  // slots: q-blocks (GQA) or pairs of q-blocks (MHA)
+  const int slo = grp >= 2 ? qlo : qlo / 2, shi = grp >= 2 ? qhi : (qhi + 1) / 2;
   const int inner = a.B * a.Hk * pairs;
   const int qbo = id / inner;
   const int rem = id % inner;
@@ -115,7 +118,7 @@ __device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, const i
   Work w;
   w.hk = (rem / pairs) % a.Hk;
   w.b = rem / (pairs * a.Hk);
-  const int qslot = nbp - 1 - qbo;
+  const int qslot = shi - 1 - qbo;
   for (int s = 0; s < 2; ++s) {
     if (grp >= 2) {
       w.head[s] = w.hk * grp + 2 * p + s;
@@ -124,9 +127,10 @@ __device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, const i
     } else {
       w.head[s] = w.hk;
       w.qbs[s] = 2 * qslot + s;
-      w.valid[s] = w.qbs[s] < NB;
+      w.valid[s] = w.qbs[s] < NB && w.qbs[s] >= qlo && w.qbs[s] < qhi;
     }
   }
+  (void)slo;
   w.n = 0;
   w.len = a.S;
   w.row0 = 0;
@@ -139,10 +143,10 @@ __device__ __forceinline__ Work decode_tile(const tasft_prefill_args& a, const i
   return w;
 }
 
-__device__ __forceinline__ int num_tiles(const tasft_prefill_args& a, int NB) {
+__host__ __device__ __forceinline__ int num_tiles(const tasft_prefill_args& a, int qlo, int qhi) {
   const int grp = a.Hq / a.Hk;
   const int pairs = grp >= 2 ? (grp + 1) / 2 : 1;
-  const int nbp = grp >= 2 ? NB : (NB + 1) / 2;
+  const int nbp = grp >= 2 ? qhi - qlo : (qhi + 1) / 2 - qlo / 2;
   return a.B * a.Hk * pairs * nbp;
 }
 
@@ -155,7 +159,8 @@ template <int D, bool kF16>
 __global__ void __launch_bounds__(kThreads, 2)
     bsa_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv, const tasft_prefill_args a, const int NB,
-                          const int32_t* cu, float* bmax, const int emulate_bf16, const int wait_pv) {
+                          const int32_t* cu, float* bmax, const int emulate_bf16, const int wait_pv, const int qlo,
+                          const int qhi) {
   using L = Smem<D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -184,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);  // [0] tmem base
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles = num_tiles(a, NB);
+  const int tiles = num_tiles(a, qlo, qhi);
   const int words = (NB + 31) / 32;
 
   if (warp == 0 && lane == 0) {
@@ -242,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         w.n = -1;
       } else {
         // ---- union of the two slots' kept lists (warp 0 only) ----
-        w = decode_tile(a, cu, NB, tile);
+        w = decode_tile(a, cu, NB, tile, qlo, qhi);
         for (int i = lane; i < 2 * words; i += 32) bitmap[(i / words) * kWords + i % words] = 0;
         __syncwarp();
         for (int s = 0; s < 2; ++s) {
@@ -582,10 +587,9 @@ int launch_tc(const tasft_prefill_args& a, const int32_t* cu, int total, cudaStr
   if (!make_tmap_bhsd(&mq, a.q, mb, a.Hq, ms, D, a.q_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
   if (!make_tmap_bhsd(&mk, a.k, mb, a.Hk, ms, D, a.k_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
   if (!make_tmap_bhsd(&mv, a.v, mb, a.Hk, ms, D, a.v_stride, es, 64)) return TASFT_ERR_UNSUPPORTED;
-  const int grp = a.Hq / a.Hk;
-  const int pairs = grp >= 2 ? (grp + 1) / 2 : 1;
-  const int nbp = grp >= 2 ? NB : (NB + 1) / 2;
-  const int64_t tiles = (int64_t)a.B * a.Hk * pairs * nbp;
+  // q-block window (qb_hi <= 0: every q-block)
+  const int qlo = a.qb_hi > 0 ? a.qb_lo : 0, qhi = a.qb_hi > 0 ? a.qb_hi : NB;
+  const int64_t tiles = num_tiles(a, qlo, qhi);
   auto kern = bsa_prefill_tc_kernel<D, kF16>;
   const int smem = Smem<D>::kAlloc;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -602,7 +606,8 @@ int launch_tc(const tasft_prefill_args& a, const int32_t* cu, int total, cudaStr
   if (grid > tiles) grid = tiles;
   if (debug_enabled()) debug_log("prefill_tc D=%d tiles=%lld grid=%lld smem=%d", D, (long long)tiles, (long long)grid, smem);
   const int wait_pv = std::getenv("TASFT_PREFILL_WAIT_PV") != nullptr;
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB, cu, bmax, emulate_bf16, wait_pv);
+  if (tiles <= 0) return TASFT_OK;
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(mq, mk, mv, a, NB, cu, bmax, emulate_bf16, wait_pv, qlo, qhi);
   count_launch();
   return launch_status();
 }
@@ -621,6 +626,7 @@ int prefill_tc(const tasft_prefill_args& a, cudaStream_t st, const int32_t* cu, 
     return TASFT_ERR_UNSUPPORTED;
   const bool f16 = a.dtype == TASFT_F16;
   if (bmax && cu) return TASFT_ERR_UNSUPPORTED;  // block maxima only for the padded layout
+  if (a.qb_hi > 0 && (cu || a.qb_lo < 0 || a.qb_lo >= a.qb_hi || a.qb_hi > NB)) return TASFT_ERR_INVALID_ARG;
   if (a.D == 128)
     return f16 ? launch_tc<128, true>(a, cu, total, st, bmax, emulate_bf16)
                : launch_tc<128, false>(a, cu, total, st, bmax, emulate_bf16);

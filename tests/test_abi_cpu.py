@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = L.lib()
-    assert lib.tasft_abi_version() == 2
+    assert lib.tasft_abi_version() == 3
     assert lib.tasft_status_string(0) == b"ok"
     assert b"argument" in lib.tasft_status_string(-1)
     assert lib.tasft_launch_count() >= 0

@@ -167,3 +167,26 @@ def test_long_prefill_qblock_ranges_sum_to_full(world):
         assert part[:, :, : lo * 64].eq(0).all() and part[:, :, hi * 64:].eq(0).all()
         acc += part.float()
     assert torch.equal(acc.to(full.dtype), full)
+
+
+@pytest.mark.parametrize("grp", [7, 1])
+def test_long_prefill_qblock_window_writes_only_its_rows(grp):
+    """q_block_range: the tensor-core kernel visits only the window's tiles. Rows inside the
+    window equal the full call bit for bit; rows outside keep what the output held (NaN
+    here). GQA (7 q-heads per kv-head) and MHA (pairs of q-blocks per tile, odd window
+    ends)."""
+    g = torch.Generator(device=DEV).manual_seed(33)
+    B, Hk, S, D = 1, 2, 4096, 128
+    Hq = Hk * grp
+    q = torch.randn(B, Hq, S, D, device=DEV, generator=g).bfloat16()
+    k = torch.randn(B, Hk, S, D, device=DEV, generator=g).bfloat16()
+    v = torch.randn(B, Hk, S, D, device=DEV, generator=g).bfloat16()
+    mask = M.prefill_mask(torch.rand(B, Hk, S // 64, S // 64, device=DEV, generator=g), 0.2)
+    kern = T.BlockSparseFlashAttention()
+    kept = T.mask_to_kept(mask, True)
+    full = kern.forward(q, k, v, kept)
+    for lo, hi in [(0, 21), (21, 47), (47, 64)]:
+        out = torch.full_like(full, float("nan"))
+        kern.forward(q, k, v, SH.restrict_qblocks(kept, lo, hi), out=out, q_block_range=(lo, hi))
+        assert torch.equal(out[:, :, lo * 64: hi * 64], full[:, :, lo * 64: hi * 64])
+        assert out[:, :, : lo * 64].isnan().all() and out[:, :, hi * 64:].isnan().all()
